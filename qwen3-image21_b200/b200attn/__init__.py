@@ -1,0 +1,257 @@
+"""Python binding of libb200attn.so (the C ABI in include/b200_attn.h) for tests and
+benchmarks.  Every compute call goes through the CUDA library; there is no fallback —
+without the built library on an sm_100 device the calls raise.
+
+Names mirror the reference's functions on this path:
+  chunked_attention      src/transformer.rs:259  (q, k, v [B,H,S,D], scale, mask)
+  attention_forward      src/transformer.rs:179-193 (the norm -> RoPE -> cat -> attention
+                         -> head-merge span of Attention::forward)
+  joint_layout           src/joint_layout.rs:52  (JointLayout::new)
+  rope_positions/rope_pe src/rope.rs:104-211     (EmbedNd)
+  key_valid_to_desc      src/transformer.rs:642-649, 736-745
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional, Sequence, Tuple
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libb200attn.so")
+HEAD_DIM = 128
+
+# b200_status
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE, ERR_LAYOUT, ERR_DEVICE_TIMEOUT = (
+    0, -1, -2, -3, -4, -5, -6)
+
+EXPORTED = (
+    "b200_attn_workspace_bytes", "b200_attn_fwd", "b200_chunked_attention", "b200_norm_rope",
+    "b200_joint_layout", "b200_rope_positions", "b200_rope_pe", "b200_key_valid_to_desc",
+    "b200_strerror", "b200_abi_version",
+)
+
+
+class B200Error(RuntimeError):
+    """A non-zero b200_status from the library."""
+
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what}: {strerror(status)} ({status})")
+
+
+class KvDesc(ctypes.Structure):
+    _fields_ = [("prefix_valid", ctypes.c_int32), ("target_valid", ctypes.c_int32)]
+
+
+class AttnArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32), ("heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+        ("target_len", ctypes.c_int32), ("prefix_len", ctypes.c_int32),
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+        ("prefix_k", ctypes.c_void_p), ("prefix_v", ctypes.c_void_p),
+        ("norm_q_w", ctypes.c_void_p), ("norm_k_w", ctypes.c_void_p),
+        ("norm_eps", ctypes.c_float), ("pe", ctypes.c_void_p), ("desc", ctypes.c_void_p),
+        ("scale", ctypes.c_float), ("out", ctypes.c_void_p), ("k_rot_out", ctypes.c_void_p),
+        ("v_out", ctypes.c_void_p), ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t), ("status", ctypes.c_void_p),
+    ]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded C-ABI library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with qwen3-image21_b200/build.py")
+        L = ctypes.CDLL(LIB_PATH)
+        vp, i32, f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_float
+        L.b200_attn_workspace_bytes.argtypes = [ctypes.POINTER(AttnArgs), ctypes.POINTER(ctypes.c_size_t)]
+        L.b200_attn_fwd.argtypes = [ctypes.POINTER(AttnArgs), vp]
+        L.b200_chunked_attention.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, vp, vp, vp]
+        L.b200_norm_rope.argtypes = [vp, vp, i32, i32, i32, i32, vp, f32, vp, vp]
+        L.b200_joint_layout.argtypes = [i32, vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]
+        L.b200_rope_positions.argtypes = [vp, i32, vp, i32, vp]
+        L.b200_rope_pe.argtypes = [vp, i32, vp, i32, vp, f32, vp]
+        L.b200_key_valid_to_desc.argtypes = [vp, i32, i32, i32, vp]
+        L.b200_strerror.argtypes = [ctypes.c_int]
+        L.b200_strerror.restype = ctypes.c_char_p
+        for name in EXPORTED:
+            if name != "b200_strerror":
+                getattr(L, name).restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def strerror(status: int) -> str:
+    return lib().b200_strerror(int(status)).decode()
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != OK:
+        raise B200Error(rc, what)
+
+
+def _np_ptr(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+# ----------------------------------------------------------------- host-side mirrors
+def joint_layout(text_len: int, text_image_mask: Optional[Sequence[bool]],
+                 cond_shapes: Sequence[Tuple[int, int]], target: Tuple[int, int]) -> dict:
+    """JointLayout::new via the C ABI: image_ids, image_pad_mask, img_shapes, lengths."""
+    tim = None if text_image_mask is None else np.ascontiguousarray(text_image_mask, np.uint8)
+    cs = np.ascontiguousarray(np.asarray(cond_shapes, np.int32).reshape(-1, 2)) if len(cond_shapes) else None
+    n_cond = 0 if cs is None else cs.shape[0]
+    ln, pl, tl = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+    shapes = np.zeros((n_cond + 1, 3), np.int32)
+    _check(lib().b200_joint_layout(text_len, _np_ptr(tim), _np_ptr(cs), n_cond, target[0], target[1],
+                                   0, None, None, _np_ptr(shapes), ctypes.byref(ln),
+                                   ctypes.byref(pl), ctypes.byref(tl)), "joint_layout")
+    ids = np.zeros(ln.value, np.int64)
+    mask = np.zeros(ln.value, np.uint8)
+    _check(lib().b200_joint_layout(text_len, _np_ptr(tim), _np_ptr(cs), n_cond, target[0], target[1],
+                                   ln.value, _np_ptr(ids), _np_ptr(mask), _np_ptr(shapes),
+                                   ctypes.byref(ln), ctypes.byref(pl), ctypes.byref(tl)), "joint_layout")
+    return dict(image_ids=ids, image_pad_mask=mask, img_shapes=[tuple(map(int, s)) for s in shapes],
+                prefix_len=pl.value, target_len=tl.value)
+
+
+def rope_positions(img_shapes, image_pad_mask) -> np.ndarray:
+    """EmbedNd position rules via the C ABI -> int64 [S, 3]."""
+    shp = np.ascontiguousarray(np.asarray(img_shapes, np.int32).reshape(-1, 3))
+    m = np.ascontiguousarray(image_pad_mask, np.uint8)
+    out = np.zeros((m.shape[0], 3), np.int64)
+    _check(lib().b200_rope_positions(_np_ptr(shp), shp.shape[0], _np_ptr(m), m.shape[0], _np_ptr(out)),
+           "rope_positions")
+    return out
+
+
+def rope_pe(img_shapes, image_pad_mask, axes=(16, 56, 56), theta: float = 1e4) -> np.ndarray:
+    """EmbedNd::new + forward via the C ABI -> float32 [S, sum(axes)]."""
+    shp = np.ascontiguousarray(np.asarray(img_shapes, np.int32).reshape(-1, 3))
+    m = np.ascontiguousarray(image_pad_mask, np.uint8)
+    ax = np.ascontiguousarray(axes, np.int32)
+    out = np.zeros((m.shape[0], int(sum(axes))), np.float32)
+    _check(lib().b200_rope_pe(_np_ptr(shp), shp.shape[0], _np_ptr(m), m.shape[0], _np_ptr(ax),
+                              float(theta), _np_ptr(out)), "rope_pe")
+    return out
+
+
+def key_valid_to_desc(key_valid: np.ndarray, prefix_len: int, target_len: int) -> np.ndarray:
+    """[B, P+T] 0/1 mask -> int32 [B, 2] descriptors (prefix_valid, target_valid)."""
+    kv = np.ascontiguousarray(key_valid, np.uint8)
+    out = np.zeros((kv.shape[0], 2), np.int32)
+    _check(lib().b200_key_valid_to_desc(_np_ptr(kv), kv.shape[0], prefix_len, target_len, _np_ptr(out)),
+           "key_valid_to_desc")
+    return out
+
+
+# ----------------------------------------------------------------- device entry points
+def _stream(stream) -> Optional[int]:
+    import torch
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def _dptr(t) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def make_args(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w, pe, out, desc=None, scale=None,
+              eps: float = 1e-6, k_rot_out=None, v_out=None, workspace=None, status=None) -> AttnArgs:
+    """Fill b200_attn_args from torch tensors (no checks beyond what the library does)."""
+    b, t, h, d = q.shape
+    p = 0 if prefix_k is None else prefix_k.shape[2]
+    a = AttnArgs()
+    a.batch, a.heads, a.head_dim, a.target_len, a.prefix_len = b, h, d, t, p
+    a.q, a.k, a.v = _dptr(q), _dptr(k), _dptr(v)
+    a.prefix_k, a.prefix_v = _dptr(prefix_k), _dptr(prefix_v)
+    a.norm_q_w, a.norm_k_w = _dptr(norm_q_w), _dptr(norm_k_w)
+    a.norm_eps = eps
+    a.pe = _dptr(pe)
+    a.desc = _dptr(desc)
+    a.scale = d ** -0.5 if scale is None else scale
+    a.out = _dptr(out)
+    a.k_rot_out, a.v_out = _dptr(k_rot_out), _dptr(v_out)
+    a.workspace = _dptr(workspace)
+    a.workspace_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    a.status = _dptr(status)
+    return a
+
+
+def workspace_bytes(args: AttnArgs) -> int:
+    n = ctypes.c_size_t()
+    _check(lib().b200_attn_workspace_bytes(ctypes.byref(args), ctypes.byref(n)), "workspace_bytes")
+    return n.value
+
+
+def attention_forward(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w, pe, desc=None, scale=None,
+                      eps: float = 1e-6, out=None, k_rot_out=None, v_out=None, workspace=None,
+                      status=None, stream=None):
+    """The Attention::forward span from the norm to the head merge on the GPU.
+
+    q, k, v: bf16 [B,T,H,D] raw projections; prefix_k/v: bf16 [B,H,P,D] (or None);
+    norm weights f32 [D]; pe f32 [T,D]; desc int32 [B,2] device tensor or None.
+    Returns out bf16 [B,T,H*D].
+    """
+    import torch
+    b, t, h, d = q.shape
+    if out is None:
+        out = torch.empty((b, t, h * d), dtype=torch.bfloat16, device=q.device)
+    args = make_args(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w, pe, out, desc, scale, eps,
+                     k_rot_out, v_out, None, status)
+    if workspace is None:
+        need = workspace_bytes(args)
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    args.workspace = workspace.data_ptr()
+    args.workspace_bytes = workspace.numel()
+    _check(lib().b200_attn_fwd(ctypes.byref(args), _stream(stream)), "b200_attn_fwd")
+    return out
+
+
+def chunked_attention(q, k, v, scale: float, mask=None, key_len=None, status=None, out=None,
+                      stream=None):
+    """chunked_attention(q, k, v, scale, mask) on [B,H,S,D] bf16 tensors.
+
+    ``mask`` is the reference's bool key mask [B,1,1,Skv] (True = attend); it must keep a
+    leading run of keys per batch row (B200Error ERR_LAYOUT otherwise).  ``key_len`` (int32
+    device tensor [B]) may be given instead.
+    """
+    import torch
+    b, h, sq, d = q.shape
+    skv = k.shape[2]
+    if mask is not None:
+        if key_len is not None:
+            raise ValueError("give mask or key_len, not both")
+        m = mask.reshape(b, -1)
+        if m.shape[1] != skv:
+            raise B200Error(ERR_LAYOUT, "chunked_attention: per-query masks are not supported")
+        m = m.to("cpu").numpy().astype(bool)
+        lens = m.sum(1)
+        for i in range(b):
+            if not m[i, :lens[i]].all():
+                raise B200Error(ERR_LAYOUT, "chunked_attention: mask is not a leading run of keys")
+        key_len = torch.tensor(lens, dtype=torch.int32, device=q.device)
+    if out is None:
+        out = torch.empty((b, h, sq, d), dtype=torch.bfloat16, device=q.device)
+    _check(lib().b200_chunked_attention(_dptr(q), _dptr(k), _dptr(v), _dptr(out), b, h, sq, skv, d,
+                                        float(scale), _dptr(key_len), _dptr(status), _stream(stream)),
+           "b200_chunked_attention")
+    return out
+
+
+def norm_rope(x, norm_w, eps: float, pe, out=None, stream=None):
+    """RMSNorm + RoPE: x bf16 [B,T,H,D] -> bf16 [B,H,T,D]."""
+    import torch
+    b, t, h, d = x.shape
+    if out is None:
+        out = torch.empty((b, h, t, d), dtype=torch.bfloat16, device=x.device)
+    _check(lib().b200_norm_rope(_dptr(x), _dptr(out), b, t, h, d, _dptr(norm_w), float(eps), _dptr(pe),
+                                _stream(stream)), "b200_norm_rope")
+    return out

@@ -1,0 +1,675 @@
+// attn_fwd.cu — B200 (sm_100a) joint-attention path of the Qwen-Image-2.1 MMDiT blocks.
+//
+// Two kernels per attention layer:
+//   norm_rope_kernel   per-head RMSNorm (eps 1e-6) + interleaved RoPE of Q and K,
+//                      token-major [B,T,H,D] -> head-major [B,H,T,D] bf16 (the K output is
+//                      the prefix-cache layout).  Reference: src/transformer.rs:179-185,
+//                      src/rope.rs:222-228.
+//   joint_attn_kernel  online-softmax attention of 256 query rows (two 128-row tiles) of
+//                      one (batch, head) over [prefix keys ; step keys].  K/V tiles of 128
+//                      keys arrive by TMA (128-byte swizzle, no multicast) into a 2-stage
+//                      ring; S = Q K^T and O += P V run on tcgen05.mma (bf16 -> f32) with
+//                      S, P and O in tensor memory; two softmax warpgroups ping-pong so the
+//                      tensor core works on one Q tile while the other is in softmax.
+//                      Masking comes from per-batch key lengths.  Reference:
+//                      chunked_attention, src/transformer.rs:259-296.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/b200_attn.h"
+#include "ptx.cuh"
+
+namespace b200 {
+
+constexpr int kD = 128;        // head_dim
+constexpr int kBM = 128;       // query rows per tile
+constexpr int kBN = 128;       // keys per K/V tile
+constexpr int kQTiles = 2;     // query tiles per CTA
+constexpr int kStages = 2;     // K and V ring depth
+constexpr int kTileBytes = kBM * kD * 2;       // 32 KiB: 128 x 128 bf16
+constexpr int kRegionBytes = 128 * 64 * 2;     // 16 KiB: 128 rows x 64 cols (one swizzle span)
+constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA, warp 2 TMEM alloc, 4-7 / 8-11 softmax
+constexpr int kSmemQ = 0;
+constexpr int kSmemK = kSmemQ + kQTiles * kTileBytes;
+constexpr int kSmemV = kSmemK + kStages * kTileBytes;
+constexpr int kSmemBar = kSmemV + kStages * kTileBytes;
+constexpr int kSmemBytes = kSmemBar + 256 + 1024;  // barriers + 1 KiB alignment slack
+constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O0 | O1, 128 columns each
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: O is rescaled when the max grows >2^8
+
+struct AttnParams {
+  int32_t T;                 // query rows
+  int32_t P;                 // rows of segment 0 (prefix cache), 0 = none
+  int32_t L1;                // rows of segment 1 (this call's keys)
+  int32_t v1_token_major;    // segment-1 V map is [B,T,H,D] (coords d, h, row, b)
+  const int32_t* seg0_len;   // valid keys of segment 0 per batch row (stride seg0_stride)
+  const int32_t* seg1_len;
+  int32_t seg0_stride, seg1_stride;
+  float scale_log2;          // scale * log2(e)
+  __nv_bfloat16* out;
+  int64_t out_sb, out_sh, out_sr;  // element strides: batch, head, query row
+  int32_t* status;
+};
+
+__device__ __forceinline__ void record_error(const AttnParams& p, volatile int* abort_flag,
+                                             int code) {
+  *abort_flag = 1;
+  if (p.status) atomicCAS(p.status, 0, code);
+}
+
+// Bounded wait that also gives up as soon as another role of the CTA has aborted.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
+                                              volatile int* abort_flag) {
+  return mbar_wait(bar, parity, abort_flag);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    joint_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
+                      const __grid_constant__ CUtensorMap tm_k0,
+                      const __grid_constant__ CUtensorMap tm_v0,
+                      const __grid_constant__ CUtensorMap tm_k1,
+                      const __grid_constant__ CUtensorMap tm_v1, const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem + kSmemQ;
+  uint8_t* sK = smem + kSmemK;
+  uint8_t* sV = smem + kSmemV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [kStages]
+  uint64_t* k_empty = bars + 3;  // [kStages]
+  uint64_t* v_full = bars + 5;   // [kStages]
+  uint64_t* v_empty = bars + 7;  // [kStages]
+  uint64_t* s_full = bars + 9;   // [kQTiles]
+  uint64_t* p_full = bars + 11;  // [kQTiles]
+  uint64_t* o_full = bars + 13;  // [kQTiles]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int q0 = blockIdx.x * (kQTiles * kBM);
+
+  // Key tiles: segment 0 (prefix) then segment 1; each segment's last tile may be ragged.
+  int pv = 0;
+  if (p.P > 0) pv = p.seg0_len ? min(max(p.seg0_len[(int64_t)b * p.seg0_stride], 0), p.P) : p.P;
+  const int tv = p.seg1_len ? min(max(p.seg1_len[(int64_t)b * p.seg1_stride], 0), p.L1) : p.L1;
+  const int n0 = (pv + kBN - 1) / kBN;
+  const int n1 = (tv + kBN - 1) / kBN;
+  const int n = n0 + n1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(k_full + s, 1);
+      mbar_init(k_empty + s, 1);
+      mbar_init(v_full + s, 1);
+      mbar_init(v_empty + s, 1);
+    }
+    for (int t = 0; t < kQTiles; ++t) {
+      mbar_init(s_full + t, 1);
+      mbar_init(p_full + t, kBM);
+      mbar_init(o_full + t, 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0 && n > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k1);
+      tma_prefetch_desc(&tm_v1);
+      if (n0 > 0) {
+        tma_prefetch_desc(&tm_k0);
+        tma_prefetch_desc(&tm_v0);
+      }
+      mbar_expect_tx(q_full, kQTiles * kTileBytes);
+      for (int t = 0; t < kQTiles; ++t)
+        for (int c = 0; c < 2; ++c)
+          tma_load_4d(sQ + t * kTileBytes + c * kRegionBytes, &tm_q, q_full, c * 64,
+                      q0 + t * kBM, h, b);
+      bool ok = true;
+      for (int j = 0; j < n && ok; ++j) {
+        const int s = j & 1;
+        const uint32_t u = static_cast<uint32_t>(j >> 1);
+        const bool seg0 = j < n0;
+        const int row = (seg0 ? j : j - n0) * kBN;
+        if (j >= kStages && !wait_or_abort(k_empty + s, (u - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(k_full + s, kTileBytes);
+        for (int c = 0; c < 2; ++c)
+          tma_load_4d(sK + s * kTileBytes + c * kRegionBytes, seg0 ? &tm_k0 : &tm_k1,
+                      k_full + s, c * 64, row, h, b);
+        if (j >= kStages && !wait_or_abort(v_empty + s, (u - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(v_full + s, kTileBytes);
+        for (int c = 0; c < 2; ++c) {
+          uint8_t* dst = sV + s * kTileBytes + c * kRegionBytes;
+          if (seg0)
+            tma_load_4d(dst, &tm_v0, v_full + s, c * 64, row, h, b);
+          else if (p.v1_token_major)
+            tma_load_4d(dst, &tm_v1, v_full + s, c * 64, h, row, b);
+          else
+            tma_load_4d(dst, &tm_v1, v_full + s, c * 64, row, h, b);
+        }
+      }
+      if (!ok) {
+        record_error(p, abort_flag, 1);
+        // Let copies already issued land before the CTA's shared memory is released.
+        for (int s = 0; s < kStages; ++s) {
+          mbar_wait(k_full + s, 0);
+          mbar_wait(v_full + s, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0 && n > 0) {
+      constexpr uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, 0, 0);
+      constexpr uint32_t idesc_pv = idesc_bf16_f32(kBM, kD, 0, 1);
+      const uint32_t sQa = smem_addr(sQ), sKa = smem_addr(sK), sVa = smem_addr(sV);
+      auto qk = [&](int t, int s) {
+        const uint32_t d = tmem_base + t * kBN;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kRegionBytes + (kk & 3) * 32;
+          const uint64_t a = smem_desc(sQa + t * kTileBytes + off, 16, 1024);
+          const uint64_t bd = smem_desc(sKa + s * kTileBytes + off, 16, 1024);
+          mma_ss(d, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto pv_mma = [&](int t, int s, bool acc) {
+        const uint32_t d = tmem_base + 2 * kBN + t * kD;
+        const uint32_t a = tmem_base + t * kBN;  // P (bf16 pairs) over S's first 64 columns
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t bd = smem_desc(sVa + s * kTileBytes + kk * 16 * 128, kRegionBytes, 1024);
+          mma_ts(d, a + kk * 8, bd, idesc_pv, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = wait_or_abort(q_full, 0, abort_flag) && wait_or_abort(k_full, 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        qk(0, 0);
+        mma_commit(s_full + 0);
+        qk(1, 0);
+        mma_commit(s_full + 1);
+        mma_commit(k_empty + 0);
+      }
+      for (int j = 0; j < n && ok; ++j) {
+        const int s = j & 1;
+        const uint32_t u = static_cast<uint32_t>(j >> 1);
+        const int s1 = (j + 1) & 1;
+        const uint32_t u1 = static_cast<uint32_t>((j + 1) >> 1);
+        const bool more = j + 1 < n;
+        if (!wait_or_abort(v_full + s, u & 1, abort_flag) ||
+            !wait_or_abort(p_full + 0, j & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        pv_mma(0, s, j > 0);
+        if (!more) mma_commit(o_full + 0);
+        if (more) {
+          if (!wait_or_abort(k_full + s1, u1 & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          qk(0, s1);
+          mma_commit(s_full + 0);
+        }
+        if (!wait_or_abort(p_full + 1, j & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        pv_mma(1, s, j > 0);
+        mma_commit(v_empty + s);
+        if (!more) mma_commit(o_full + 1);
+        if (more) {
+          qk(1, s1);
+          mma_commit(s_full + 1);
+          mma_commit(k_empty + s1);
+        }
+      }
+      if (!ok) record_error(p, abort_flag, 2);
+    }
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- softmax / epilogue
+    const int t = (warp - 4) >> 2;
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem_base + lane_off + t * kBN;
+    const uint32_t tO = tmem_base + lane_off + 2 * kBN + t * kD;
+    const float c = p.scale_log2;
+    float m = -INFINITY;  // running max, scaled (log2) units
+    float l = 0.f;        // running sum of p
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (!wait_or_abort(s_full + t, j & 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[4][32];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tmem_ld32(tS + q * 32, r[q]);
+      tmem_wait_ld();
+      const int valid = j < n0 ? min(kBN, pv - j * kBN) : min(kBN, tv - (j - n0) * kBN);
+      float mx = -INFINITY;
+      if (valid < kBN) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (q * 32 + i >= valid) r[q][i] = __float_as_uint(-INFINITY);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[q][i]));
+      const float mx_s = mx * c;
+      float alpha = 1.f;
+      if (mx_s > m + kRescaleThreshold) {
+        alpha = ex2_approx(m - mx_s);  // 0 on the first tile (m = -inf)
+        m = mx_s;
+      }
+      const float neg_m = -m;
+      float sum = 0.f;
+      uint32_t pk[2][32];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(r[q][i]), c, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(r[q][i + 1]), c, neg_m));
+          sum += p0 + p1;
+          pk[q >> 1][(q & 1) * 16 + (i >> 1)] = pack_bf16x2(p0, p1);
+        }
+      tmem_st32(tS, pk[0]);
+      tmem_st32(tS + 32, pk[1]);
+      l = l * alpha + sum;
+      // O rescale: PV of the previous tile is complete (s_full is committed after it).
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t o[32];
+          tmem_ld32(tO + q * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + q * 32, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full + t);
+    }
+    if (!ok) record_error(p, abort_flag, 3);
+    // Epilogue: O / l -> bf16 rows of `out`.
+    const int qrow = q0 + t * kBM + row;
+    const bool store = qrow < p.T;
+    __nv_bfloat16* dst = p.out + b * p.out_sb + h * p.out_sh + static_cast<int64_t>(qrow) * p.out_sr;
+    if (n == 0) {
+      // No valid key: the reference's softmax over an all -inf row is NaN.
+      if (store) {
+        const uint4 nan4 = make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
+        for (int i = 0; i < kD / 8; ++i) reinterpret_cast<uint4*>(dst)[i] = nan4;
+      }
+    } else if (ok) {
+      if (!wait_or_abort(o_full + t, 0, abort_flag)) {
+        record_error(p, abort_flag, 4);
+      } else {
+        tc_fence_after();
+        const float inv_l = 1.f / l;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t o[32];
+          tmem_ld32(tO + q * 32, o);
+          tmem_wait_ld();
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            w[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv_l,
+                               __uint_as_float(o[2 * i + 1]) * inv_l);
+          if (store) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + q * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ norm + RoPE
+// One warp per (b, t, h) row of 128 values; lane i owns elements 4i..4i+3 (RoPE pairs
+// 2i and 2i+1).  y = RoPE(x / sqrt(mean(x^2) + eps) * w), computed in f32, rounded once.
+struct NormRopeJob {
+  const __nv_bfloat16* x;
+  __nv_bfloat16* y;
+  const float* w;  // NULL: no norm
+};
+
+__global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeJob j0, NormRopeJob j1,
+                                                         NormRopeJob j2, int B, int T, int H,
+                                                         float eps, const float* pe,
+                                                         int rope_mask) {
+  const NormRopeJob job = blockIdx.y == 0 ? j0 : (blockIdx.y == 1 ? j1 : j2);
+  const bool rope = pe != nullptr && ((rope_mask >> blockIdx.y) & 1);
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = static_cast<int64_t>(B) * T * H;
+  if (row >= rows) return;
+  const int h = static_cast<int>(row % H);
+  const int t = static_cast<int>((row / H) % T);
+  const int b = static_cast<int>(row / (static_cast<int64_t>(H) * T));
+  const uint2 raw = *reinterpret_cast<const uint2*>(job.x + row * kD + lane * 4);
+  const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+  const __nv_bfloat162 c2 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+  float v0 = __bfloat162float(a.x), v1 = __bfloat162float(a.y);
+  float v2 = __bfloat162float(c2.x), v3 = __bfloat162float(c2.y);
+  if (job.w) {
+    float ss = v0 * v0 + v1 * v1 + v2 * v2 + v3 * v3;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float den = sqrtf(ss / static_cast<float>(kD) + eps);
+    const float4 w4 = *reinterpret_cast<const float4*>(job.w + lane * 4);
+    v0 = v0 / den * w4.x;
+    v1 = v1 / den * w4.y;
+    v2 = v2 / den * w4.z;
+    v3 = v3 / den * w4.w;
+  }
+  if (rope) {
+    const float4 cs = *reinterpret_cast<const float4*>(pe + static_cast<int64_t>(t) * kD + lane * 4);
+    const float r0 = v0 * cs.x - v1 * cs.y, r1 = v0 * cs.y + v1 * cs.x;
+    const float r2 = v2 * cs.z - v3 * cs.w, r3 = v2 * cs.w + v3 * cs.z;
+    v0 = r0; v1 = r1; v2 = r2; v3 = r3;
+  }
+  const __nv_bfloat162 o01 = __floats2bfloat162_rn(v0, v1);
+  const __nv_bfloat162 o23 = __floats2bfloat162_rn(v2, v3);
+  uint2 outv;
+  outv.x = *reinterpret_cast<const uint32_t*>(&o01);
+  outv.y = *reinterpret_cast<const uint32_t*>(&o23);
+  const int64_t drow = (static_cast<int64_t>(b) * H + h) * T + t;
+  *reinterpret_cast<uint2*>(job.y + drow * kD + lane * 4) = outv;
+}
+
+// ------------------------------------------------------------------ host helpers
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 4-D map over a bf16 tensor with 128 columns per row and a 64 x 128-row box, 128-byte
+// swizzle, zero fill outside the tensor.  head_major: [B,H,rows,128] with coordinates
+// (d, row, h, b); otherwise token-major [B,rows,H,128] with coordinates (d, h, row, b).
+int make_map(CUtensorMap* map, const void* base, int B, int H, int rows, bool head_major) {
+  auto fn = encode_fn();
+  if (!fn) return B200_ERR_CUDA;
+  cuuint64_t dims[4];
+  cuuint64_t strides[3];
+  cuuint32_t box[4];
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const cuuint64_t row_bytes = kD * 2;
+  if (head_major) {
+    dims[0] = kD; dims[1] = rows; dims[2] = H; dims[3] = B;
+    strides[0] = row_bytes;
+    strides[1] = row_bytes * rows;
+    strides[2] = row_bytes * rows * H;
+    box[0] = 64; box[1] = kBN; box[2] = 1; box[3] = 1;
+  } else {
+    dims[0] = kD; dims[1] = H; dims[2] = rows; dims[3] = B;
+    strides[0] = row_bytes;
+    strides[1] = row_bytes * H;
+    strides[2] = row_bytes * H * rows;
+    box[0] = 64; box[1] = 1; box[2] = kBN; box[3] = 1;
+  }
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B200_OK : B200_ERR_CUDA;
+}
+
+std::mutex g_attr_mutex;
+bool g_attr_done[64] = {};
+
+int ensure_kernel_attrs() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B200_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  if (dev >= 0 && dev < 64 && g_attr_done[dev]) return B200_OK;
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0) return B200_ERR_UNSUPPORTED;
+  if (cudaFuncSetAttribute(joint_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kSmemBytes) != cudaSuccess)
+    return B200_ERR_CUDA;
+  if (dev >= 0 && dev < 64) g_attr_done[dev] = true;
+  return B200_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+int launch_attention(const CUtensorMap& mq, const CUtensorMap& mk0, const CUtensorMap& mv0,
+                     const CUtensorMap& mk1, const CUtensorMap& mv1, const AttnParams& prm,
+                     int B, int H, int T, cudaStream_t stream) {
+  int rc = ensure_kernel_attrs();
+  if (rc != B200_OK) return rc;
+  dim3 grid((T + kQTiles * kBM - 1) / (kQTiles * kBM), H, B);
+  joint_attn_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk0, mv0, mk1, mv1, prm);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+int launch_norm_rope(const NormRopeJob* jobs, int njobs, int B, int T, int H, float eps,
+                     const float* pe, int rope_mask, cudaStream_t stream) {
+  const int64_t rows = static_cast<int64_t>(B) * T * H;
+  if (rows == 0 || njobs == 0) return B200_OK;
+  const int64_t blocks = (rows + 7) / 8;
+  if (blocks > 0x7fffffff) return B200_ERR_INVALID;
+  NormRopeJob j[3] = {jobs[0], njobs > 1 ? jobs[1] : jobs[0], njobs > 2 ? jobs[2] : jobs[0]};
+  dim3 grid(static_cast<unsigned>(blocks), njobs);
+  norm_rope_kernel<<<grid, 256, 0, stream>>>(j[0], j[1], j[2], B, T, H, eps, pe, rope_mask);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+// Attention of post-RoPE q [B,H,T,D] over [prefix (B,H,P,D) ; step k_rot (B,H,T,D) and
+// v (B,T,H,D, token-major)], out [B,T,H*D].  Arguments are already validated.
+int joint_attention(const void* q_rot, const void* k_rot, const void* v, const void* prefix_k,
+                    const void* prefix_v, int B, int H, int T, int P, const b200_kv_desc* desc,
+                    float scale, void* out, int32_t* status, cudaStream_t stream) {
+  CUtensorMap mq{}, mk0{}, mv0{}, mk1{}, mv1{};
+  int rc;
+  if ((rc = make_map(&mq, q_rot, B, H, T, true)) != B200_OK) return rc;
+  if ((rc = make_map(&mk1, k_rot, B, H, T, true)) != B200_OK) return rc;
+  if ((rc = make_map(&mv1, v, B, H, T, false)) != B200_OK) return rc;
+  if (P > 0) {
+    if ((rc = make_map(&mk0, prefix_k, B, H, P, true)) != B200_OK) return rc;
+    if ((rc = make_map(&mv0, prefix_v, B, H, P, true)) != B200_OK) return rc;
+  }
+  AttnParams prm{};
+  prm.T = T;
+  prm.P = P;
+  prm.L1 = T;
+  prm.v1_token_major = 1;
+  prm.seg0_len = desc ? &desc[0].prefix_valid : nullptr;
+  prm.seg1_len = desc ? &desc[0].target_valid : nullptr;
+  prm.seg0_stride = 2;
+  prm.seg1_stride = 2;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.out_sb = static_cast<int64_t>(T) * H * kD;
+  prm.out_sh = kD;
+  prm.out_sr = static_cast<int64_t>(H) * kD;
+  prm.status = status;
+  return launch_attention(mq, mk0, mv0, mk1, mv1, prm, B, H, T, stream);
+}
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" int b200_attn_workspace_bytes(const b200_attn_args* a, size_t* bytes) {
+  if (!a || !bytes) return B200_ERR_INVALID;
+  if (a->batch < 0 || a->heads < 0 || a->target_len < 0) return B200_ERR_INVALID;
+  const size_t tensor = static_cast<size_t>(a->batch) * a->heads * a->target_len * kD * 2;
+  size_t need = round_up(tensor, 256);               // post-RoPE Q
+  if (!a->k_rot_out) need += round_up(tensor, 256);  // post-RoPE K
+  *bytes = need;
+  return B200_OK;
+}
+
+extern "C" int b200_attn_fwd(const b200_attn_args* a, b200_stream_t stream_) {
+  if (!a) return B200_ERR_INVALID;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (a->head_dim != kD) return B200_ERR_UNSUPPORTED;
+  if (a->batch <= 0 || a->heads <= 0 || a->target_len < 0 || a->prefix_len < 0)
+    return B200_ERR_INVALID;
+  if (a->target_len == 0) return B200_OK;
+  if (!a->q || !a->k || !a->v || !a->out || !a->norm_q_w || !a->norm_k_w || !a->pe)
+    return B200_ERR_INVALID;
+  if (a->prefix_len > 0 && (!a->prefix_k || !a->prefix_v)) return B200_ERR_INVALID;
+  if (!(a->scale > 0.f) || !std::isfinite(a->scale)) return B200_ERR_INVALID;
+  const void* ptrs[] = {a->q, a->k, a->v, a->out, a->norm_q_w, a->norm_k_w, a->pe,
+                        a->workspace, a->k_rot_out, a->v_out, a->prefix_k, a->prefix_v};
+  for (const void* ptr : ptrs)
+    if (ptr && !aligned16(ptr)) return B200_ERR_INVALID;
+  size_t need = 0;
+  b200_attn_workspace_bytes(a, &need);
+  if (!a->workspace || a->workspace_bytes < need) return B200_ERR_WORKSPACE;
+
+  const int B = a->batch, H = a->heads, T = a->target_len, P = a->prefix_len;
+  const size_t tensor = static_cast<size_t>(B) * H * T * kD * 2;
+  auto* ws = static_cast<uint8_t*>(a->workspace);
+  auto* q_rot = reinterpret_cast<__nv_bfloat16*>(ws);
+  auto* k_rot = a->k_rot_out ? static_cast<__nv_bfloat16*>(a->k_rot_out)
+                             : reinterpret_cast<__nv_bfloat16*>(ws + round_up(tensor, 256));
+
+  NormRopeJob jobs[3] = {
+      {static_cast<const __nv_bfloat16*>(a->q), q_rot, a->norm_q_w},
+      {static_cast<const __nv_bfloat16*>(a->k), k_rot, a->norm_k_w},
+      {static_cast<const __nv_bfloat16*>(a->v), static_cast<__nv_bfloat16*>(a->v_out), nullptr}};
+  int rc = launch_norm_rope(jobs, a->v_out ? 3 : 2, B, T, H, a->norm_eps, a->pe, 0x3, stream);
+  if (rc != B200_OK) return rc;
+
+  return joint_attention(q_rot, k_rot, a->v, a->prefix_k, a->prefix_v, B, H, T, P, a->desc,
+                         a->scale, a->out, a->status, stream);
+}
+
+extern "C" int b200_joint_attention(const void* q_rot, const void* k_rot, const void* v,
+                                    const void* prefix_k, const void* prefix_v, int32_t batch,
+                                    int32_t heads, int32_t target_len, int32_t prefix_len,
+                                    int32_t head_dim, const b200_kv_desc* desc, float scale,
+                                    void* out, int32_t* status, b200_stream_t stream) {
+  if (head_dim != kD) return B200_ERR_UNSUPPORTED;
+  if (batch <= 0 || heads <= 0 || target_len < 0 || prefix_len < 0) return B200_ERR_INVALID;
+  if (target_len == 0) return B200_OK;
+  if (!q_rot || !k_rot || !v || !out) return B200_ERR_INVALID;
+  if (prefix_len > 0 && (!prefix_k || !prefix_v)) return B200_ERR_INVALID;
+  const void* ptrs[] = {q_rot, k_rot, v, out, prefix_k, prefix_v};
+  for (const void* ptr : ptrs)
+    if (ptr && !aligned16(ptr)) return B200_ERR_INVALID;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return B200_ERR_INVALID;
+  return joint_attention(q_rot, k_rot, v, prefix_k, prefix_v, batch, heads, target_len,
+                         prefix_len, desc, scale, out, status, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b200_chunked_attention(const void* q, const void* k, const void* v, void* out,
+                                      int32_t batch, int32_t heads, int32_t sq, int32_t skv,
+                                      int32_t head_dim, float scale, const int32_t* key_len,
+                                      int32_t* status, b200_stream_t stream_) {
+  if (head_dim != kD) return B200_ERR_UNSUPPORTED;
+  if (batch <= 0 || heads <= 0 || sq < 0 || skv <= 0) return B200_ERR_INVALID;
+  if (sq == 0) return B200_OK;
+  if (!q || !k || !v || !out) return B200_ERR_INVALID;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return B200_ERR_INVALID;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return B200_ERR_INVALID;
+  CUtensorMap mq{}, mk0{}, mv0{}, mk1{}, mv1{};
+  int rc;
+  if ((rc = make_map(&mq, q, batch, heads, sq, true)) != B200_OK) return rc;
+  if ((rc = make_map(&mk1, k, batch, heads, skv, true)) != B200_OK) return rc;
+  if ((rc = make_map(&mv1, v, batch, heads, skv, true)) != B200_OK) return rc;
+  AttnParams prm{};
+  prm.T = sq;
+  prm.P = 0;
+  prm.L1 = skv;
+  prm.v1_token_major = 0;
+  prm.seg1_len = key_len;
+  prm.seg1_stride = 1;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.out_sb = static_cast<int64_t>(heads) * sq * kD;
+  prm.out_sh = static_cast<int64_t>(sq) * kD;
+  prm.out_sr = kD;
+  prm.status = status;
+  return launch_attention(mq, mk0, mv0, mk1, mv1, prm, batch, heads, sq,
+                          static_cast<cudaStream_t>(stream_));
+}
+
+extern "C" int b200_norm_rope(const void* x, void* y, int32_t batch, int32_t tokens,
+                              int32_t heads, int32_t head_dim, const float* norm_w, float eps,
+                              const float* pe, b200_stream_t stream) {
+  if (head_dim != kD) return B200_ERR_UNSUPPORTED;
+  if (batch < 0 || tokens < 0 || heads < 0) return B200_ERR_INVALID;
+  if (!x || !y || !aligned16(x) || !aligned16(y)) return B200_ERR_INVALID;
+  if ((norm_w && !aligned16(norm_w)) || (pe && !aligned16(pe))) return B200_ERR_INVALID;
+  NormRopeJob job{static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), norm_w};
+  return launch_norm_rope(&job, 1, batch, tokens, heads, eps, pe, 0x1,
+                          static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,135 @@
+"""The C-ABI library without a GPU: it loads, exports every symbol include/b200_attn.h
+declares, its host-side mirrors reproduce the reference's known answers and the oracle,
+and its entry points reject bad arguments before touching a device."""
+import ctypes
+import json
+import os
+import re
+
+import numpy as np
+import pytest
+
+import b200attn
+from oracle import reference as ref
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def declared_functions():
+    src = open(os.path.join(ROOT, "include", "b200_attn.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(b200_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    names = declared_functions()
+    assert len(names) >= 10
+    lib = b200attn.lib()
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/b200_attn.h but not exported"
+    assert set(names) <= set(b200attn.EXPORTED) | {"b200_attn_fwd_noalloc"}
+    assert lib.b200_abi_version() == 1
+
+
+def test_strerror():
+    assert b200attn.strerror(0) == "ok"
+    for code in range(-6, 0):
+        assert b200attn.strerror(code) != "unknown status"
+
+
+@pytest.mark.parametrize("case", json.load(open(os.path.join(GOLDEN, "layout_kat.json"))),
+                         ids=lambda c: c["source"])
+def test_joint_layout_kat_through_abi(case):
+    cs = [tuple(s) for s in case["cond_shapes"]]
+    lay = b200attn.joint_layout(case["text_len"], case["text_image_mask"], cs, tuple(case["target"]))
+    if "image_ids" in case:
+        assert lay["image_ids"].tolist() == case["image_ids"]
+        assert (lay["prefix_len"], lay["target_len"]) == (case["prefix_len"], case["target_len"])
+    else:
+        assert lay["image_ids"][:8].tolist() == case["image_ids_prefix8"]
+
+
+def test_joint_layout_errors_through_abi():
+    with pytest.raises(b200attn.B200Error):
+        b200attn.joint_layout(2, [True, False], [], (2, 2))
+    with pytest.raises(b200attn.B200Error):
+        b200attn.joint_layout(2, [True, True], [(4, 4)], (2, 2))
+    with pytest.raises(b200attn.B200Error):
+        b200attn.joint_layout(3, [False] * 3, [(2, 2)], (2, 2))
+
+
+def test_rope_kat_through_abi():
+    kat = json.load(open(os.path.join(GOLDEN, "rope_kat.json")))
+    pe = b200attn.rope_pe(kat["img_shapes"], kat["image_pad_mask"], kat["axes"], kat["theta"])
+    assert np.max(np.abs(pe - np.asarray(kat["rows"], np.float32))) < kat["tol"]
+    pos = b200attn.rope_positions(kat["img_shapes"], kat["image_pad_mask"])
+    assert pos.tolist() == kat["positions"]
+
+
+@pytest.mark.parametrize("text,cond,target", [
+    (512, [], (64, 64)),                       # config 2 layout (1024^2 T2I)
+    (256, [], (32, 32)),                       # config 1 layout (512^2)
+    (40, [(4, 6), (8, 8)], (6, 10)),           # two condition images in the prompt
+])
+def test_rope_pe_matches_oracle(text, cond, target):
+    slots = [False] * text
+    p = 2
+    for (h, w) in cond:  # place each image's slots after a couple of text tokens
+        n = h * w // 4
+        slots[p:p + n] = [True] * n
+        p += n + 2
+    lay = ref.joint_layout(text, slots, cond, target)
+    want = ref.embed_nd(lay["img_shapes"], lay["image_pad_mask"])
+    got = b200attn.rope_pe(lay["img_shapes"], lay["image_pad_mask"])
+    # both build the tables in f32; one-ulp differences of inv_freq grow with the
+    # position (angles up to ~600 rad here), well inside the reference KAT's 1e-3
+    assert np.max(np.abs(got - want)) < 1e-4
+    assert np.array_equal(b200attn.rope_positions(lay["img_shapes"], lay["image_pad_mask"]),
+                          ref.rope_positions(lay["img_shapes"], lay["image_pad_mask"]))
+    lay2 = b200attn.joint_layout(text, slots, cond, target)
+    assert lay2["image_ids"].tolist() == lay["image_ids"]
+
+
+def test_rope_pe_rejects_positions_outside_table():
+    # a 9000-token prompt runs past the reference's 8191 table end
+    with pytest.raises(b200attn.B200Error):
+        b200attn.rope_pe([(1, 2, 2)], [0] * 9000 + [1] * 4)
+
+
+def test_key_valid_to_desc_through_abi():
+    kv = np.ones((2, 20), np.uint8)
+    kv[0, 10:15] = 0
+    assert b200attn.key_valid_to_desc(kv, 15, 5).tolist() == [[10, 5], [15, 5]]
+    kv[1, 3] = 0
+    with pytest.raises(b200attn.B200Error):
+        b200attn.key_valid_to_desc(kv, 15, 5)
+
+
+def test_entry_points_reject_bad_arguments_without_device():
+    lib = b200attn.lib()
+    a = b200attn.AttnArgs()
+    a.batch, a.heads, a.head_dim, a.target_len = 1, 1, 64, 8
+    assert lib.b200_attn_fwd(ctypes.byref(a), None) == b200attn.ERR_UNSUPPORTED
+    a.head_dim = 128
+    assert lib.b200_attn_fwd(ctypes.byref(a), None) == b200attn.ERR_INVALID  # null tensors
+    a.target_len = 0
+    assert lib.b200_attn_fwd(ctypes.byref(a), None) == b200attn.OK  # nothing to do
+    assert lib.b200_attn_fwd(None, None) == b200attn.ERR_INVALID
+    assert lib.b200_chunked_attention(None, None, None, None, 1, 1, 4, 4, 96, 0.1, None, None,
+                                      None) == b200attn.ERR_UNSUPPORTED
+    assert lib.b200_chunked_attention(None, None, None, None, 1, 1, 4, 4, 128, 0.1, None, None,
+                                      None) == b200attn.ERR_INVALID
+    assert lib.b200_norm_rope(None, None, 1, 1, 1, 128, None, 1e-6, None, None) == b200attn.ERR_INVALID
+    # misaligned (but non-null) pointers are refused before any device access
+    assert lib.b200_chunked_attention(8, 16, 32, 48, 1, 1, 4, 4, 128, 0.1, None, None,
+                                      None) == b200attn.ERR_INVALID
+
+
+def test_workspace_bytes():
+    a = b200attn.AttnArgs()
+    a.batch, a.heads, a.head_dim, a.target_len = 1, 32, 128, 4096
+    n = b200attn.workspace_bytes(a)
+    assert n == 2 * 32 * 4096 * 128 * 2
+    a.k_rot_out = 256
+    assert b200attn.workspace_bytes(a) == 32 * 4096 * 128 * 2

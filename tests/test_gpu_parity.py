@@ -1,0 +1,248 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle.
+
+Tolerances (bf16 output against the reference's f32 path):
+relative L2 <= 5e-3 and max-abs <= 2e-2.  Small cases compare every element with the
+oracle; the full-size configurations compare a sample of query rows and check
+size-independent properties (softmax weights sum to one, linearity in V)."""
+import os
+
+import numpy as np
+import pytest
+
+import b200attn
+from oracle import reference as ref
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 5e-3
+MAX_ABS = 2e-2
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def bf16(t):
+    return t.to(_torch().bfloat16)
+
+
+def f32np(t):
+    return t.float().cpu().numpy()
+
+
+def check(got, want, rel=REL_L2, mx=MAX_ABS):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    assert np.isfinite(got).all()
+    r = ref.rel_l2(got, want)
+    m = float(np.max(np.abs(got - want))) if got.size else 0.0
+    assert r <= rel and m <= mx, f"rel_l2={r:.3e} max_abs={m:.3e}"
+    return r, m
+
+
+def make_case(B, T, H, P, seed, device, pv=None, layout_text=None):
+    torch = _torch()
+    g = torch.Generator().manual_seed(seed)
+    q = bf16(torch.randn(B, T, H, 128, generator=g))
+    k = bf16(torch.randn(B, T, H, 128, generator=g))
+    v = bf16(torch.randn(B, T, H, 128, generator=g))
+    pk = bf16(torch.randn(B, H, P, 128, generator=g)) if P else None
+    pvv = bf16(torch.randn(B, H, P, 128, generator=g)) if P else None
+    wq = (1 + 0.1 * torch.randn(128, generator=g)).float()
+    wk = (1 + 0.1 * torch.randn(128, generator=g)).float()
+    # target grid as close to square as T allows, behind a `text`-token prompt
+    hgt = int(np.sqrt(T))
+    while T % hgt:
+        hgt -= 1
+    text = P if layout_text is None else layout_text
+    lay = ref.joint_layout(text, None, [], (hgt, T // hgt))
+    pe = ref.embed_nd(lay["img_shapes"], lay["image_pad_mask"])[text:]
+    desc = None
+    if pv is not None:
+        desc = np.array([(x, T) for x in pv], np.int32)
+    dev = dict(q=q.to(device), k=k.to(device), v=v.to(device),
+               pk=None if pk is None else pk.to(device), pv=None if pvv is None else pvv.to(device),
+               wq=wq.to(device), wk=wk.to(device), pe=torch.from_numpy(pe).to(device),
+               desc=None if desc is None else torch.from_numpy(desc).to(device))
+    host = dict(q=f32np(q), k=f32np(k), v=f32np(v), pk=None if pk is None else f32np(pk),
+                pv=None if pvv is None else f32np(pvv), wq=wq.numpy(), wk=wk.numpy(), pe=pe,
+                desc=None if desc is None else [tuple(x) for x in desc])
+    return dev, host
+
+
+def run_gpu(d, **kw):
+    return b200attn.attention_forward(d["q"], d["k"], d["v"], d["pk"], d["pv"], d["wq"], d["wk"],
+                                      d["pe"], desc=d["desc"], **kw)
+
+
+def run_oracle(h):
+    prefix = None if h["pk"] is None else (h["pk"], h["pv"])
+    return ref.attention_forward(h["q"], h["k"], h["v"], h["wq"], h["wk"], h["pe"], prefix, h["desc"])
+
+
+# ------------------------------------------------------------------ prologue
+def test_norm_rope_matches_oracle(cuda):
+    torch = _torch()
+    d, h = make_case(2, 300, 3, 0, 11, cuda)
+    y = b200attn.norm_rope(d["q"], d["wq"], 1e-6, d["pe"])
+    torch.cuda.synchronize()
+    want = ref.apply_rope(np.transpose(ref.rms_norm(h["q"], h["wq"]), (0, 2, 1, 3)), h["pe"])
+    # one bf16 rounding of the f32 result: <= 2^-8 relative per element
+    assert np.max(np.abs(f32np(y) - want) / (np.abs(want) + 1e-3)) < 2 ** -8 + 1e-6
+    check(f32np(y), want, rel=3e-3)
+
+
+# ------------------------------------------------------------------ plain attention
+@pytest.mark.parametrize("B,H,sq,skv", [
+    (1, 1, 128, 128), (1, 2, 256, 256), (2, 3, 1, 1), (1, 2, 37, 300), (2, 1, 300, 129),
+    (1, 4, 500, 1000), (1, 1, 257, 2000),
+])
+def test_chunked_attention_matches_oracle(cuda, B, H, sq, skv):
+    torch = _torch()
+    g = torch.Generator().manual_seed(B * 7 + H * 13 + sq + skv)
+    q = bf16(torch.randn(B, H, sq, 128, generator=g))
+    k = bf16(torch.randn(B, H, skv, 128, generator=g))
+    v = bf16(torch.randn(B, H, skv, 128, generator=g))
+    out = b200attn.chunked_attention(q.to(cuda), k.to(cuda), v.to(cuda), 128 ** -0.5)
+    torch.cuda.synchronize()
+    want = ref.chunked_attention(f32np(q), f32np(k), f32np(v), 128 ** -0.5)
+    check(f32np(out), want)
+
+
+def test_chunked_attention_key_mask(cuda):
+    torch = _torch()
+    g = torch.Generator().manual_seed(5)
+    B, H, sq, skv = 3, 2, 200, 400
+    q = bf16(torch.randn(B, H, sq, 128, generator=g))
+    k = bf16(torch.randn(B, H, skv, 128, generator=g))
+    v = bf16(torch.randn(B, H, skv, 128, generator=g))
+    mask = torch.zeros(B, 1, 1, skv, dtype=torch.bool)
+    for b, n in enumerate([1, 129, 400]):
+        mask[b, ..., :n] = True
+    out = b200attn.chunked_attention(q.to(cuda), k.to(cuda), v.to(cuda), 128 ** -0.5, mask=mask.to(cuda))
+    torch.cuda.synchronize()
+    want = ref.chunked_attention(f32np(q), f32np(k), f32np(v), 128 ** -0.5, mask.numpy())
+    check(f32np(out), want)
+    bad = mask.clone()
+    bad[0, ..., 5] = True  # hole -> not a leading run of keys
+    with pytest.raises(b200attn.B200Error):
+        b200attn.chunked_attention(q.to(cuda), k.to(cuda), v.to(cuda), 128 ** -0.5, mask=bad.to(cuda))
+
+
+def test_chunked_attention_scale_and_large_logits(cuda):
+    """Logits far above 1 exercise the running-max rescale of O."""
+    torch = _torch()
+    g = torch.Generator().manual_seed(9)
+    q = bf16(4 * torch.randn(1, 2, 256, 128, generator=g))
+    k = bf16(4 * torch.randn(1, 2, 1024, 128, generator=g))
+    v = bf16(torch.randn(1, 2, 1024, 128, generator=g))
+    out = b200attn.chunked_attention(q.to(cuda), k.to(cuda), v.to(cuda), 0.25)
+    torch.cuda.synchronize()
+    want = ref.chunked_attention(f32np(q), f32np(k), f32np(v), 0.25)
+    check(f32np(out), want)
+
+
+# ------------------------------------------------------------------ the full span
+def test_golden_fixture(cuda):
+    torch = _torch()
+    g = np.load(os.path.join(GOLDEN, "attn_small.npz"))
+
+    def t(name):
+        a = g[name]
+        if a.dtype == np.uint16:
+            return torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16).to(cuda)
+        return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+    B, T, H, _ = g["q"].shape
+    k_rot = torch.empty(B, H, T, 128, dtype=torch.bfloat16, device=cuda)
+    v_out = torch.empty(B, H, T, 128, dtype=torch.bfloat16, device=cuda)
+    out = b200attn.attention_forward(t("q"), t("k"), t("v"), t("prefix_k"), t("prefix_v"),
+                                     t("norm_q_w"), t("norm_k_w"), t("pe"), desc=t("desc"),
+                                     k_rot_out=k_rot, v_out=v_out)
+    torch.cuda.synchronize()
+    check(f32np(out), g["out"])
+    check(f32np(k_rot), g["k_rot"], rel=3e-3)
+    v_ref = np.transpose((g["v"].astype(np.uint32) << 16).view(np.float32), (0, 2, 1, 3))
+    assert np.array_equal(f32np(v_out), v_ref)
+
+
+@pytest.mark.parametrize("B,T,H,P,pv", [
+    (1, 1024, 32, 256, None),         # config 1 (512^2): 1024 queries over 256 + 1024 keys
+    (1, 200, 4, 300, [263]),          # ragged prefix (config 3 shape in miniature)
+    (2, 130, 2, 0, None),             # no prefix cache
+    (2, 77, 3, 129, [1, 129]),        # one valid prefix key; full prefix
+    (1, 64, 2, 40, [0]),              # every prefix key padded
+])
+def test_attention_forward_matches_oracle(cuda, B, T, H, P, pv):
+    torch = _torch()
+    d, h = make_case(B, T, H, P, 1000 + T + P, cuda, pv=pv)
+    out = run_gpu(d)
+    torch.cuda.synchronize()
+    want, _, _ = run_oracle(h)
+    check(f32np(out), want)
+
+
+def test_attention_forward_is_deterministic_and_status_clear(cuda):
+    torch = _torch()
+    d, _ = make_case(1, 1024, 8, 256, 77, cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    a = run_gpu(d, status=status)
+    b = run_gpu(d, status=status)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert int(status.item()) == 0
+
+
+# ------------------------------------------------------------------ full sizes
+def _sampled_rows_check(out, h, rows):
+    """Oracle on a subset of query rows (attention rows are independent)."""
+    sub = dict(h)
+    sub["q"] = h["q"][:, rows]
+    sub["pe_q"] = h["pe"][rows]
+    b, t, hh, d = h["q"].shape
+    q = np.transpose(ref.rms_norm(sub["q"], h["wq"]), (0, 2, 1, 3))
+    q = ref.apply_rope(q, sub["pe_q"])
+    k = ref.apply_rope(np.transpose(ref.rms_norm(h["k"], h["wk"]), (0, 2, 1, 3)), h["pe"])
+    v = np.transpose(h["v"], (0, 2, 1, 3))
+    k_all = np.concatenate([h["pk"], k], 2)
+    v_all = np.concatenate([h["pv"], v], 2)
+    mask = None
+    if h["desc"] is not None:
+        p = h["pk"].shape[2]
+        mask = np.zeros((b, 1, 1, p + t), bool)
+        for i, (pv_, tv_) in enumerate(h["desc"]):
+            mask[i, ..., :pv_] = True
+            mask[i, ..., p:p + tv_] = True
+    o = ref.chunked_attention(q, k_all, v_all, 128 ** -0.5, mask)
+    want = np.transpose(o, (0, 2, 1, 3)).reshape(b, len(rows), hh * d)
+    check(f32np(out)[:, rows], want)
+
+
+@pytest.mark.parametrize("T,P,pv", [
+    (4096, 512, None),        # config 2 (1024^2 T2I)
+    (4096, 10624, [10587]),   # config 3 (edit with two condition images, 37 padded keys)
+])
+def test_full_size_configs(cuda, T, P, pv):
+    torch = _torch()
+    d, h = make_case(1, T, 32, P, 2000 + P, cuda, pv=pv, layout_text=512)
+    out = run_gpu(d)
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(T + P)
+    rows = np.sort(rng.choice(T, 48, replace=False))
+    _sampled_rows_check(out, h, rows)
+    # linearity in V (size independent): attn(2 v) == 2 attn(v) exactly in bf16
+    d2 = dict(d)
+    d2["v"] = d["v"] * 2
+    d2["pv"] = d["pv"] * 2
+    out2 = run_gpu(d2)
+    torch.cuda.synchronize()
+    assert torch.equal(out2, out * 2)
+    # constant V rows -> every output equals that constant (weights sum to one)
+    d3 = dict(d)
+    d3["v"] = torch.full_like(d["v"], 0.75)
+    d3["pv"] = torch.full_like(d["pv"], 0.75)
+    out3 = run_gpu(d3)
+    torch.cuda.synchronize()
+    assert float((out3.float() - 0.75).abs().max()) < 4e-3
