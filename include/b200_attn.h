@@ -141,6 +141,16 @@ int b200_norm_rope(const void* x, void* y, int32_t batch, int32_t tokens, int32_
                    int32_t head_dim, const float* norm_w, float eps, const float* pe,
                    b200_stream_t stream);
 
+/*
+ * The prologue b200_attn_fwd launches: RMSNorm + RoPE of Q and K in one kernel.
+ * q, k device [B,T,H,D] bf16 -> q_rot, k_rot device [B,H,T,D] bf16; norm weights device
+ * [D] f32; pe device [T,D] f32.  With b200_joint_attention it splits b200_attn_fwd into
+ * its two launches (src/transformer.rs:179-185).
+ */
+int b200_qk_norm_rope(const void* q, const void* k, void* q_rot, void* k_rot, int32_t batch,
+                      int32_t tokens, int32_t heads, int32_t head_dim, const float* norm_q_w,
+                      const float* norm_k_w, float eps, const float* pe, b200_stream_t stream);
+
 /* ---- host-side mirrors of the reference's layout / RoPE / mask code (no device) ---- */
 
 /*

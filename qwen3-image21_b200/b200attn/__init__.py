@@ -27,7 +27,8 @@ OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE, ERR_LAYOUT, ERR_DEVIC
     0, -1, -2, -3, -4, -5, -6)
 
 EXPORTED = (
-    "b200_attn_workspace_bytes", "b200_attn_fwd", "b200_chunked_attention", "b200_norm_rope",
+    "b200_attn_workspace_bytes", "b200_attn_fwd", "b200_joint_attention", "b200_chunked_attention",
+    "b200_norm_rope", "b200_qk_norm_rope",
     "b200_joint_layout", "b200_rope_positions", "b200_rope_pe", "b200_key_valid_to_desc",
     "b200_strerror", "b200_abi_version",
 )
@@ -74,6 +75,9 @@ def lib() -> ctypes.CDLL:
         L.b200_attn_fwd.argtypes = [ctypes.POINTER(AttnArgs), vp]
         L.b200_chunked_attention.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, vp, vp, vp]
         L.b200_norm_rope.argtypes = [vp, vp, i32, i32, i32, i32, vp, f32, vp, vp]
+        L.b200_qk_norm_rope.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, vp, vp, f32, vp, vp]
+        L.b200_joint_attention.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, f32, vp,
+                                           vp, vp]
         L.b200_joint_layout.argtypes = [i32, vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]
         L.b200_rope_positions.argtypes = [vp, i32, vp, i32, vp]
         L.b200_rope_pe.argtypes = [vp, i32, vp, i32, vp, f32, vp]
@@ -254,4 +258,35 @@ def norm_rope(x, norm_w, eps: float, pe, out=None, stream=None):
         out = torch.empty((b, h, t, d), dtype=torch.bfloat16, device=x.device)
     _check(lib().b200_norm_rope(_dptr(x), _dptr(out), b, t, h, d, _dptr(norm_w), float(eps), _dptr(pe),
                                 _stream(stream)), "b200_norm_rope")
+    return out
+
+
+def qk_norm_rope(q, k, norm_q_w, norm_k_w, eps: float, pe, q_rot=None, k_rot=None, stream=None):
+    """The b200_attn_fwd prologue alone: RMSNorm + RoPE of q and k in one launch.
+    q, k bf16 [B,T,H,D] -> (q_rot, k_rot) bf16 [B,H,T,D]."""
+    import torch
+    b, t, h, d = q.shape
+    if q_rot is None:
+        q_rot = torch.empty((b, h, t, d), dtype=torch.bfloat16, device=q.device)
+    if k_rot is None:
+        k_rot = torch.empty((b, h, t, d), dtype=torch.bfloat16, device=q.device)
+    _check(lib().b200_qk_norm_rope(_dptr(q), _dptr(k), _dptr(q_rot), _dptr(k_rot), b, t, h, d,
+                                   _dptr(norm_q_w), _dptr(norm_k_w), float(eps), _dptr(pe),
+                                   _stream(stream)), "b200_qk_norm_rope")
+    return q_rot, k_rot
+
+
+def joint_attention(q_rot, k_rot, v, prefix_k, prefix_v, desc=None, scale=None, out=None,
+                    status=None, stream=None):
+    """The attention launch of b200_attn_fwd: post-RoPE q_rot/k_rot bf16 [B,H,T,D], v bf16
+    [B,T,H,D], prefix bf16 [B,H,P,D] or None -> out bf16 [B,T,H*D]."""
+    import torch
+    b, h, t, d = q_rot.shape
+    p = 0 if prefix_k is None else prefix_k.shape[2]
+    if out is None:
+        out = torch.empty((b, t, h * d), dtype=torch.bfloat16, device=q_rot.device)
+    _check(lib().b200_joint_attention(_dptr(q_rot), _dptr(k_rot), _dptr(v), _dptr(prefix_k),
+                                      _dptr(prefix_v), b, h, t, p, d, _dptr(desc),
+                                      float(d ** -0.5 if scale is None else scale), _dptr(out),
+                                      _dptr(status), _stream(stream)), "b200_joint_attention")
     return out

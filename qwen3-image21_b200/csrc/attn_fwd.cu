@@ -75,6 +75,125 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// ---- packed f32x2 arithmetic (sm_100 FFMA2 / FADD2: two lanes per instruction)
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x0, 2^x1 on the FMA pipe instead of the MUFU: x = j + f with j = rint(x) (taken from
+// the low mantissa bits of x + 1.5*2^23) and f in [-1/2, 1/2]; 2^f by a degree-4
+// polynomial with relative error < 3e-6 (coefficients from csrc/exp2_poly_fit.py); 2^j
+// applied by adding j to the exponent field.  x is clamped at -126.5 so j >= -126 (the
+// result is then at most ~1e-38 instead of 0, far below any row sum, which is >= 1).
+constexpr float kExpC1 = 6.931241751e-01f;
+constexpr float kExpC2 = 2.402409911e-01f;
+constexpr float kExpC3 = 5.590642616e-02f;
+constexpr float kExpC4 = 9.582848288e-03f;
+__device__ __forceinline__ void exp2_fma2(float x0, float x1, float& y0, float& y1) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const uint64_t x = f2pack(fmaxf(x0, -126.5f), fmaxf(x1, -126.5f));
+  const uint64_t t = f2add(x, f2pack(kMagic, kMagic));
+  const uint64_t j = f2add(t, f2pack(-kMagic, -kMagic));
+  const uint64_t f = f2fma(j, f2pack(-1.f, -1.f), x);
+  uint64_t a = f2fma(f2pack(kExpC4, kExpC4), f, f2pack(kExpC3, kExpC3));
+  a = f2fma(a, f, f2pack(kExpC2, kExpC2));
+  a = f2fma(a, f, f2pack(kExpC1, kExpC1));
+  a = f2fma(a, f, f2pack(1.f, 1.f));
+  float a0, a1, t0, t1;
+  f2unpack(a, a0, a1);
+  f2unpack(t, t0, t1);
+  y0 = __int_as_float(__float_as_int(a0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(a1) + (__float_as_int(t1) << 23));
+}
+
+// One in kPolyEvery exp2 pairs of a full (unmasked) tile runs on the FMA pipe, the rest on
+// the MUFU: at D = 128 the MUFU alone needs as many cycles per tile as the tensor core.
+constexpr int kPolyEvery = 4;
+
+// Softmax of this thread's 128-key S row (TMEM columns [tS, tS + 128), one row per
+// thread): keys >= valid are masked (kMasked); the running max m (log2 units) is raised
+// only when the row max exceeds it by more than kRescaleThreshold (lazy rescaling, as in
+// FlashAttention-4), so P = 2^(S*c - m) <= 2^8.  P goes to TMEM columns [tS, tS + 64) as
+// bf16 pairs, over S columns already read.  Updates the running sum l and returns the
+// factor the O accumulator must be scaled by (1 when m did not move).
+template <bool kMasked>
+__device__ __forceinline__ float softmax_row(const int valid, const float c, float& m, float& l,
+                                             const uint32_t tS) {
+  uint32_t r[4][32];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) tmem_ld32(tS + q * 32, r[q]);
+  tmem_wait_ld();
+  auto v = [&](int col) { return __uint_as_float(r[col >> 5][col & 31]); };
+  if (kMasked) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (q * 32 + i >= valid) r[q][i] = __float_as_uint(-INFINITY);
+  }
+  float pm[8];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) pm[g] = fmaxf(v(g * 16), v(g * 16 + 1));
+#pragma unroll
+  for (int i = 1; i < 8; ++i)
+#pragma unroll
+    for (int g = 0; g < 8; ++g) pm[g] = fmax3(pm[g], v(g * 16 + 2 * i), v(g * 16 + 2 * i + 1));
+  const float mx =
+      fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])) * c;
+  float alpha = 1.f;
+  if (mx > m + kRescaleThreshold) {
+    alpha = ex2_approx(m - mx);  // 0 on the first tile (m = -inf)
+    m = mx;
+  }
+  const uint64_t cc = f2pack(c, c);
+  const uint64_t nm = f2pack(-m, -m);
+  uint64_t acc[4] = {f2pack(0.f, 0.f), f2pack(0.f, 0.f), f2pack(0.f, 0.f), f2pack(0.f, 0.f)};
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    uint32_t pk[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int col = half * 64 + 2 * i;
+      float x0, x1, p0, p1;
+      f2unpack(f2fma(f2pack(v(col), v(col + 1)), cc, nm), x0, x1);
+      if (!kMasked && (i % kPolyEvery) == kPolyEvery - 1) {
+        exp2_fma2(x0, x1, p0, p1);
+      } else {
+        p0 = ex2_approx(x0);
+        p1 = ex2_approx(x1);
+      }
+      acc[i & 3] = f2add(acc[i & 3], f2pack(p0, p1));
+      pk[i] = pack_bf16x2(p0, p1);
+    }
+    tmem_st32(tS + half * 32, pk);
+  }
+  float s[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) f2unpack(acc[i], s[2 * i], s[2 * i + 1]);
+  l = l * alpha + (((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7])));
+  return alpha;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     joint_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_k0,
@@ -139,6 +258,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  if (warp < 4) {
+  // Register split: warpgroup 0 (load, MMA, allocator) gives registers to the two softmax
+  // warpgroups; 128 x 56 + 256 x 224 = 384 x 168, the launch allocation.  Each
+  // setmaxnreg dominates the code of its role.
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0 && n > 0) {
@@ -197,25 +321,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && n > 0) {
       constexpr uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = idesc_bf16_f32(kBM, kD, 0, 1);
-      const uint32_t sQa = smem_addr(sQ), sKa = smem_addr(sK), sVa = smem_addr(sV);
+      // Descriptors as (low, high) words: a k-step only moves the start address (low 14
+      // bits, 16-byte units, < 2^14 inside the 256 KiB shared window), so the offset is
+      // added to the low word and never carries into the other fields.
+      const uint64_t dQ = smem_desc(smem_addr(sQ), 16, 1024);
+      const uint64_t dK = smem_desc(smem_addr(sK), 16, 1024);
+      const uint64_t dV = smem_desc(smem_addr(sV), kRegionBytes, 1024);
+      const uint32_t hi_qk = static_cast<uint32_t>(dQ >> 32);
+      const uint32_t hi_v = static_cast<uint32_t>(dV >> 32);
+      const uint32_t lo_q = static_cast<uint32_t>(dQ), lo_k = static_cast<uint32_t>(dK);
+      const uint32_t lo_v = static_cast<uint32_t>(dV);
       auto qk = [&](int t, int s) {
         const uint32_t d = tmem_base + t * kBN;
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kRegionBytes + (kk & 3) * 32;
-          const uint64_t a = smem_desc(sQa + t * kTileBytes + off, 16, 1024);
-          const uint64_t bd = smem_desc(sKa + s * kTileBytes + off, 16, 1024);
-          mma_ss(d, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
-        }
+        const uint32_t a = lo_q + ((t * kTileBytes) >> 4);
+        const uint32_t bk = lo_k + ((s * kTileBytes) >> 4);
+        // k-step kk: region kk/4 (16 KiB apart), 32 bytes per step inside the swizzle span
+        mma_ss_off<0, 0>(d, a, hi_qk, bk, hi_qk, idesc_qk, 0u);
+        mma_ss_off<2, 2>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+        mma_ss_off<4, 4>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+        mma_ss_off<6, 6>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+        mma_ss_off<1024, 1024>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+        mma_ss_off<1026, 1026>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+        mma_ss_off<1028, 1028>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+        mma_ss_off<1030, 1030>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
       };
       auto pv_mma = [&](int t, int s, bool acc) {
         const uint32_t d = tmem_base + 2 * kBN + t * kD;
         const uint32_t a = tmem_base + t * kBN;  // P (bf16 pairs) over S's first 64 columns
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t bd = smem_desc(sVa + s * kTileBytes + kk * 16 * 128, kRegionBytes, 1024);
-          mma_ts(d, a + kk * 8, bd, idesc_pv, (acc || kk > 0) ? 1u : 0u);
-        }
+        const uint32_t bv = lo_v + ((s * kTileBytes) >> 4);
+        // k-step kk: 16 keys = 2 KiB of V rows; P columns kk*8 .. kk*8+7
+        mma_ts_off<0>(d, a, bv, hi_v, idesc_pv, acc ? 1u : 0u);
+        mma_ts_off<128>(d, a + 8, bv, hi_v, idesc_pv, 1u);
+        mma_ts_off<256>(d, a + 16, bv, hi_v, idesc_pv, 1u);
+        mma_ts_off<384>(d, a + 24, bv, hi_v, idesc_pv, 1u);
+        mma_ts_off<512>(d, a + 32, bv, hi_v, idesc_pv, 1u);
+        mma_ts_off<640>(d, a + 40, bv, hi_v, idesc_pv, 1u);
+        mma_ts_off<768>(d, a + 48, bv, hi_v, idesc_pv, 1u);
+        mma_ts_off<896>(d, a + 56, bv, hi_v, idesc_pv, 1u);
       };
       bool ok = wait_or_abort(q_full, 0, abort_flag) && wait_or_abort(k_full, 0, abort_flag);
       if (ok) {
@@ -265,7 +407,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) record_error(p, abort_flag, 2);
     }
-  } else if (warp >= 4) {
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
     // ---------------------------------------------------------------- softmax / epilogue
     const int t = (warp - 4) >> 2;
     const int wq = warp & 3;
@@ -283,44 +427,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t r[4][32];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) tmem_ld32(tS + q * 32, r[q]);
-      tmem_wait_ld();
       const int valid = j < n0 ? min(kBN, pv - j * kBN) : min(kBN, tv - (j - n0) * kBN);
-      float mx = -INFINITY;
-      if (valid < kBN) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (q * 32 + i >= valid) r[q][i] = __float_as_uint(-INFINITY);
-      }
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[q][i]));
-      const float mx_s = mx * c;
-      float alpha = 1.f;
-      if (mx_s > m + kRescaleThreshold) {
-        alpha = ex2_approx(m - mx_s);  // 0 on the first tile (m = -inf)
-        m = mx_s;
-      }
-      const float neg_m = -m;
-      float sum = 0.f;
-      uint32_t pk[2][32];
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(r[q][i]), c, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(r[q][i + 1]), c, neg_m));
-          sum += p0 + p1;
-          pk[q >> 1][(q & 1) * 16 + (i >> 1)] = pack_bf16x2(p0, p1);
-        }
-      tmem_st32(tS, pk[0]);
-      tmem_st32(tS + 32, pk[1]);
-      l = l * alpha + sum;
+      const float alpha = valid < kBN ? softmax_row<true>(valid, c, m, l, tS)
+                                      : softmax_row<false>(valid, c, m, l, tS);
       // O rescale: PV of the previous tile is complete (s_full is committed after it).
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
@@ -384,56 +493,98 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ norm + RoPE
-// One warp per (b, t, h) row of 128 values; lane i owns elements 4i..4i+3 (RoPE pairs
-// 2i and 2i+1).  y = RoPE(x / sqrt(mean(x^2) + eps) * w), computed in f32, rounded once.
+// A group of 16 lanes handles kNormRows consecutive (b, t, h) rows of 128 values; lane i
+// of the group owns elements 8i..8i+7 (RoPE pairs 4i..4i+3) and all loads of the group's
+// rows are issued before any arithmetic.  y = RoPE(x / sqrt(mean(x^2) + eps) * w) in f32,
+// rounded to bf16 once; y is written head-major.
 struct NormRopeJob {
   const __nv_bfloat16* x;
   __nv_bfloat16* y;
   const float* w;  // NULL: no norm
 };
 
+constexpr int kNormRows = 4;
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
 __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeJob j0, NormRopeJob j1,
                                                          NormRopeJob j2, int B, int T, int H,
                                                          float eps, const float* pe,
                                                          int rope_mask) {
+  // Host guarantees B * T * H < 2^31, so row indices fit 32 bits.
   const NormRopeJob job = blockIdx.y == 0 ? j0 : (blockIdx.y == 1 ? j1 : j2);
   const bool rope = pe != nullptr && ((rope_mask >> blockIdx.y) & 1);
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  const int64_t rows = static_cast<int64_t>(B) * T * H;
-  if (row >= rows) return;
-  const int h = static_cast<int>(row % H);
-  const int t = static_cast<int>((row / H) % T);
-  const int b = static_cast<int>(row / (static_cast<int64_t>(H) * T));
-  const uint2 raw = *reinterpret_cast<const uint2*>(job.x + row * kD + lane * 4);
-  const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-  const __nv_bfloat162 c2 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-  float v0 = __bfloat162float(a.x), v1 = __bfloat162float(a.y);
-  float v2 = __bfloat162float(c2.x), v3 = __bfloat162float(c2.y);
-  if (job.w) {
-    float ss = v0 * v0 + v1 * v1 + v2 * v2 + v3 * v3;
+  const int sub = lane & 15;
+  const unsigned half_mask = lane < 16 ? 0x0000ffffu : 0xffff0000u;
+  const uint32_t group = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  const uint32_t rows = static_cast<uint32_t>(B) * T * H;
+  const uint32_t r0 = group * kNormRows;
+  if (r0 >= rows) return;  // the whole 16-lane group leaves together
+  uint4 xv[kNormRows];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float den = sqrtf(ss / static_cast<float>(kD) + eps);
-    const float4 w4 = *reinterpret_cast<const float4*>(job.w + lane * 4);
-    v0 = v0 / den * w4.x;
-    v1 = v1 / den * w4.y;
-    v2 = v2 / den * w4.z;
-    v3 = v3 / den * w4.w;
+  for (int i = 0; i < kNormRows; ++i)
+    xv[i] = r0 + i < rows ? *reinterpret_cast<const uint4*>(job.x + static_cast<size_t>(r0 + i) * kD + sub * 8)
+                          : make_uint4(0, 0, 0, 0);
+  float w[8];
+  if (job.w) {
+    const float4 wa = *reinterpret_cast<const float4*>(job.w + sub * 8);
+    const float4 wb = *reinterpret_cast<const float4*>(job.w + sub * 8 + 4);
+    w[0] = wa.x; w[1] = wa.y; w[2] = wa.z; w[3] = wa.w;
+    w[4] = wb.x; w[5] = wb.y; w[6] = wb.z; w[7] = wb.w;
   }
-  if (rope) {
-    const float4 cs = *reinterpret_cast<const float4*>(pe + static_cast<int64_t>(t) * kD + lane * 4);
-    const float r0 = v0 * cs.x - v1 * cs.y, r1 = v0 * cs.y + v1 * cs.x;
-    const float r2 = v2 * cs.z - v3 * cs.w, r3 = v2 * cs.w + v3 * cs.z;
-    v0 = r0; v1 = r1; v2 = r2; v3 = r3;
+  // (b, t, h) of row r0; later rows step h, then t, then b.
+  uint32_t h = r0 % H, bt = r0 / H;
+  uint32_t t = bt % T, b = bt / T;
+#pragma unroll
+  for (int i = 0; i < kNormRows; ++i) {
+    const uint32_t row = r0 + i;
+    float v[8];
+    bf16x8_to_f32(xv[i], v);
+    if (job.w) {
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(half_mask, ss, o);
+      const float inv = 1.f / sqrtf(ss / static_cast<float>(kD) + eps);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = v[e] * inv * w[e];
+    }
+    if (row < rows) {
+      if (rope) {
+        const float* pr = pe + static_cast<size_t>(t) * kD + sub * 8;
+        const float4 ca = *reinterpret_cast<const float4*>(pr);
+        const float4 cb = *reinterpret_cast<const float4*>(pr + 4);
+        const float cs[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float x0 = v[2 * q], x1 = v[2 * q + 1];
+          const float co = cs[2 * q], si = cs[2 * q + 1];
+          v[2 * q] = x0 * co - x1 * si;
+          v[2 * q + 1] = x0 * si + x1 * co;
+        }
+      }
+      uint4 o;
+      o.x = pack_bf16x2(v[0], v[1]);
+      o.y = pack_bf16x2(v[2], v[3]);
+      o.z = pack_bf16x2(v[4], v[5]);
+      o.w = pack_bf16x2(v[6], v[7]);
+      const size_t drow = (static_cast<size_t>(b) * H + h) * T + t;
+      *reinterpret_cast<uint4*>(job.y + drow * kD + sub * 8) = o;
+    }
+    if (++h == static_cast<uint32_t>(H)) {
+      h = 0;
+      if (++t == static_cast<uint32_t>(T)) { t = 0; ++b; }
+    }
   }
-  const __nv_bfloat162 o01 = __floats2bfloat162_rn(v0, v1);
-  const __nv_bfloat162 o23 = __floats2bfloat162_rn(v2, v3);
-  uint2 outv;
-  outv.x = *reinterpret_cast<const uint32_t*>(&o01);
-  outv.y = *reinterpret_cast<const uint32_t*>(&o23);
-  const int64_t drow = (static_cast<int64_t>(b) * H + h) * T + t;
-  *reinterpret_cast<uint2*>(job.y + drow * kD + lane * 4) = outv;
 }
 
 // ------------------------------------------------------------------ host helpers
@@ -520,7 +671,9 @@ int launch_norm_rope(const NormRopeJob* jobs, int njobs, int B, int T, int H, fl
                      const float* pe, int rope_mask, cudaStream_t stream) {
   const int64_t rows = static_cast<int64_t>(B) * T * H;
   if (rows == 0 || njobs == 0) return B200_OK;
-  const int64_t blocks = (rows + 7) / 8;
+  if (rows >= (int64_t{1} << 31)) return B200_ERR_INVALID;
+  const int64_t groups = (rows + kNormRows - 1) / kNormRows;  // 16 threads each
+  const int64_t blocks = (groups * 16 + 255) / 256;
   if (blocks > 0x7fffffff) return B200_ERR_INVALID;
   NormRopeJob j[3] = {jobs[0], njobs > 1 ? jobs[1] : jobs[0], njobs > 2 ? jobs[2] : jobs[0]};
   dim3 grid(static_cast<unsigned>(blocks), njobs);
@@ -671,5 +824,21 @@ extern "C" int b200_norm_rope(const void* x, void* y, int32_t batch, int32_t tok
   if ((norm_w && !aligned16(norm_w)) || (pe && !aligned16(pe))) return B200_ERR_INVALID;
   NormRopeJob job{static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), norm_w};
   return launch_norm_rope(&job, 1, batch, tokens, heads, eps, pe, 0x1,
+                          static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b200_qk_norm_rope(const void* q, const void* k, void* q_rot, void* k_rot,
+                                 int32_t batch, int32_t tokens, int32_t heads,
+                                 int32_t head_dim, const float* norm_q_w, const float* norm_k_w,
+                                 float eps, const float* pe, b200_stream_t stream) {
+  if (head_dim != kD) return B200_ERR_UNSUPPORTED;
+  if (batch < 0 || tokens < 0 || heads < 0) return B200_ERR_INVALID;
+  const void* ptrs[] = {q, k, q_rot, k_rot, norm_q_w, norm_k_w, pe};
+  for (const void* ptr : ptrs)
+    if (!ptr || !aligned16(ptr)) return B200_ERR_INVALID;
+  NormRopeJob jobs[2] = {
+      {static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(q_rot), norm_q_w},
+      {static_cast<const __nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(k_rot), norm_k_w}};
+  return launch_norm_rope(jobs, 2, batch, tokens, heads, eps, pe, 0x3,
                           static_cast<cudaStream_t>(stream));
 }
