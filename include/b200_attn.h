@@ -104,6 +104,25 @@ int b200_attn_workspace_bytes(const b200_attn_args* args, size_t* bytes);
 int b200_attn_fwd(const b200_attn_args* args, b200_stream_t stream);
 
 /*
+ * b200_attn_fwd without a workspace, for callers that cannot allocate device memory
+ * when they call (a frozen or foreign allocator, a plugin host that only hands over
+ * the input and output tensors).  No counterpart in the reference: it has no such
+ * constraint, candle allocates on every call.
+ *
+ * The scratch (post-RoPE Q, and K when k_rot_out is NULL) lives in a fixed device array
+ * of B200_NOALLOC_SCRATCH_BYTES inside the library, held by every GPU that loads it
+ * until exit; args->workspace and args->workspace_bytes are ignored.  Problems whose
+ * b200_attn_workspace_bytes() exceeds the limit return B200_ERR_WORKSPACE (e.g. with
+ * B = 1, H = 32: up to T = 4096 tokens with k_rot_out NULL, 8192 with it given).
+ * The first call on a device looks up the array's device address (no allocation);
+ * make that first call before any stream capture.  All calls on a device share the
+ * one array: calls that may overlap on the GPU (other streams, other threads) race
+ * on it, so serialise them.  Nothing in it needs clearing between calls.
+ */
+#define B200_NOALLOC_SCRATCH_BYTES (64u << 20)
+int b200_attn_fwd_noalloc(const b200_attn_args* args, b200_stream_t stream);
+
+/*
  * The attention part of b200_attn_fwd, for callers that already hold post-norm,
  * post-RoPE Q and K: q_rot device [B,H,T,D], k_rot device [B,H,T,D] (head-major, the
  * cache layout), v device [B,T,H,D] (token-major projection output), prefix_k/prefix_v

@@ -842,3 +842,47 @@ extern "C" int b200_qk_norm_rope(const void* q, const void* k, void* q_rot, void
   return launch_norm_rope(jobs, 2, batch, tokens, heads, eps, pe, 0x3,
                           static_cast<cudaStream_t>(stream));
 }
+
+// ------------------------------------------------------------------ no-allocation entry
+// For callers that cannot allocate device memory at call time — e.g. an engine whose
+// allocator is frozen or owned by another runtime, a plugin host that hands out only
+// the input and output tensors, or code between a memory-pool snapshot and its
+// replay — b200_attn_fwd_noalloc runs the same two kernels with the scratch taken from
+// this file-scope device array instead of a caller workspace.  Every GPU that loads
+// the library holds the array until the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[B200_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mutex;
+void* g_noalloc_scratch_ptr[64] = {};  // device address of g_noalloc_scratch, per device
+}  // namespace
+
+extern "C" int b200_attn_fwd_noalloc(const b200_attn_args* args, b200_stream_t stream) {
+  if (!args) return B200_ERR_INVALID;
+  size_t need = 0;
+  int rc = b200_attn_workspace_bytes(args, &need);
+  if (rc != B200_OK) return rc;
+  if (need > B200_NOALLOC_SCRATCH_BYTES) return B200_ERR_WORKSPACE;  // over the fixed limit
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B200_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return B200_ERR_UNSUPPORTED;
+  void* scratch = nullptr;
+  {
+    // One-time set-up per device (with that device current): the host-side name of the
+    // array is only a stand-in, so the kernels get its device address.
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_scratch_ptr[dev]) {
+      void* ptr = nullptr;
+      if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr)
+        return B200_ERR_CUDA;
+      g_noalloc_scratch_ptr[dev] = ptr;
+    }
+    scratch = g_noalloc_scratch_ptr[dev];
+  }
+  // Nothing in the scratch needs clearing: every byte the attention kernel reads from it
+  // (post-RoPE Q, and K when k_rot_out is NULL) is written by the prologue of this call.
+  b200_attn_args a = *args;
+  a.workspace = scratch;
+  a.workspace_bytes = B200_NOALLOC_SCRATCH_BYTES;
+  return b200_attn_fwd(&a, stream);
+}
