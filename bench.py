@@ -31,11 +31,31 @@ for _p in (ROOT, os.path.join(ROOT, "qwen3-image21_b200")):
 
 HEADS, HEAD_DIM = 32, 128
 CONFIGS = {
-    # name: (target grid, prefix length, prefix_valid, layers)
-    "c1": dict(grid=(32, 32), P=256, pv=None, layers=32, name="512^2 T2I (config 1)"),
-    "c2": dict(grid=(64, 64), P=512, pv=None, layers=32, name="1024^2 T2I (config 2)"),
-    "c3": dict(grid=(64, 64), P=10624, pv=10587, layers=32, name="1024^2 edit, 2 refs (config 3)"),
+    # target grid, prefix length, valid prefix keys, blocks per step, condition images
+    "c1": dict(grid=(32, 32), P=256, pv=None, layers=32, cond=[], name="512^2 T2I (config 1)"),
+    "c2": dict(grid=(64, 64), P=512, pv=None, layers=32, cond=[], name="1024^2 T2I (config 2)"),
+    # two 64x64-latent condition images fill 2 x 1024 prompt slots (4 latent tokens per slot)
+    # plus 2432 other prompt tokens: a 10624-token prefix with its last 37 keys padded
+    "c3": dict(grid=(64, 64), P=10624, pv=10587, layers=32, cond=[(64, 64), (64, 64)],
+               name="1024^2 edit, 2 refs (config 3)"),
 }
+
+
+def prompt_layout(cfg):
+    """(text_len, image-slot mask, condition shapes) whose joint prefix has cfg['P'] tokens."""
+    cond = cfg["cond"]
+    image_tokens = sum(h * w for h, w in cond)
+    other = cfg["P"] - image_tokens
+    if not cond:
+        return other, None, []
+    slots = []
+    lead = min(100, other // (len(cond) + 1))
+    used = 0
+    for h, w in cond:
+        slots += [False] * lead + [True] * (h * w // 4)
+        used += lead
+    slots += [False] * (other - used)
+    return len(slots), slots, cond
 METRIC = "attn TFLOP/s at 1024^2 (config 2), 32 blocks per denoising step"
 FALLBACK_PEAKS = dict(bf16_tflops=1590.0, bf16_tflops_sustained=1400.0, hbm_gbs=6650.0)
 
@@ -236,7 +256,9 @@ def main():
     # ---- synthetic workload (independent generation per rank), resident in HBM
     g = torch.Generator(device=dev).manual_seed(1234 + 2 + 1000 * rank)
     randn = lambda *shape: torch.randn(*shape, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
-    lay = b200attn.joint_layout(P, None, [], (gh, gw))
+    text_len, slots, cond = prompt_layout(cfg)
+    lay = b200attn.joint_layout(text_len, slots, cond, (gh, gw))
+    assert lay["prefix_len"] == P
     pe = torch.from_numpy(b200attn.rope_pe(lay["img_shapes"], lay["image_pad_mask"])[P:]).to(dev)
     ones = torch.ones(HEAD_DIM, device=dev, dtype=torch.float32)
     layers = []
@@ -251,6 +273,7 @@ def main():
     k_rot = torch.empty_like(q_rot)
     out = torch.empty(1, T, HEADS * HEAD_DIM, dtype=torch.bfloat16, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
+    split_ws = torch.empty(b200attn.SPLIT_WORKSPACE_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
     def step(marks=None):
@@ -259,7 +282,7 @@ def main():
             if marks is not None:
                 marks[li][0].record(stream)
             b200attn.joint_attention(q_rot, k_rot, ly["v"], ly["pk"], ly["pv"], desc=desc, out=out,
-                                     status=status, stream=stream)
+                                     workspace=split_ws, status=status, stream=stream)
             if marks is not None:
                 marks[li][1].record(stream)
 
@@ -299,7 +322,8 @@ def main():
         dq = torch.empty_like(layers[0]["q"])
         dk = torch.empty_like(dq)
         dv = torch.empty_like(dq)
-        ws = torch.empty(2 * T * HEADS * HEAD_DIM * 2 + 512, dtype=torch.uint8, device=dev)
+        ws = torch.empty(2 * T * HEADS * HEAD_DIM * 2 + b200attn.SPLIT_WORKSPACE_BYTES + 512,
+                         dtype=torch.uint8, device=dev)
 
         def e2e_step():
             for li, ly in enumerate(layers):

@@ -90,8 +90,16 @@ typedef struct {
                           ran out (1 = load, 2 = mma, 3 = softmax, 4 = epilogue)   */
 } b200_attn_args;
 
-/* Scratch bytes b200_attn_fwd needs for these args (post-RoPE Q, and K unless
- * k_rot_out is given).  Replaces nothing in the reference (candle allocates). */
+/*
+ * Bytes of the region that lets the attention kernel split its last partial wave of
+ * work across the idle SMs (partial results of up to 160 pieces + arrival counters).
+ */
+#define B200_ATTN_SPLIT_WORKSPACE_BYTES 21299968u
+
+/* Scratch bytes b200_attn_fwd wants for these args: post-RoPE Q, K unless k_rot_out is
+ * given, and B200_ATTN_SPLIT_WORKSPACE_BYTES for the tail split.  A workspace without
+ * the split region (B200_ATTN_SPLIT_WORKSPACE_BYTES less) is accepted and runs without
+ * the split.  Replaces nothing in the reference (candle allocates). */
 int b200_attn_workspace_bytes(const b200_attn_args* args, size_t* bytes);
 
 /*
@@ -112,8 +120,10 @@ int b200_attn_fwd(const b200_attn_args* args, b200_stream_t stream);
  * The scratch (post-RoPE Q, and K when k_rot_out is NULL) lives in a fixed device array
  * of B200_NOALLOC_SCRATCH_BYTES inside the library, held by every GPU that loads it
  * until exit; args->workspace and args->workspace_bytes are ignored.  Problems whose
- * b200_attn_workspace_bytes() exceeds the limit return B200_ERR_WORKSPACE (e.g. with
- * B = 1, H = 32: up to T = 4096 tokens with k_rot_out NULL, 8192 with it given).
+ * required scratch (b200_attn_workspace_bytes() less B200_ATTN_SPLIT_WORKSPACE_BYTES)
+ * exceeds the limit return B200_ERR_WORKSPACE (e.g. with B = 1, H = 32: up to T = 4096
+ * tokens with k_rot_out NULL, 8192 with it given); the tail split is used when its
+ * region also fits.
  * The first call on a device looks up the array's device address (no allocation);
  * make that first call before any stream capture.  All calls on a device share the
  * one array: calls that may overlap on the GPU (other streams, other threads) race
@@ -127,14 +137,17 @@ int b200_attn_fwd_noalloc(const b200_attn_args* args, b200_stream_t stream);
  * post-RoPE Q and K: q_rot device [B,H,T,D], k_rot device [B,H,T,D] (head-major, the
  * cache layout), v device [B,T,H,D] (token-major projection output), prefix_k/prefix_v
  * device [B,H,P,D] (NULL if P = 0), desc device [B] or NULL; out device [B,T,H*D].
- * Replaces Tensor::cat + chunked_attention + transpose/reshape
- * (src/transformer.rs:186-193, src/quantized_transformer.rs:145-151).  One kernel.
+ * workspace: device, >= B200_ATTN_SPLIT_WORKSPACE_BYTES to enable the tail split, or
+ * NULL.  Replaces Tensor::cat + chunked_attention + transpose/reshape
+ * (src/transformer.rs:186-193, src/quantized_transformer.rs:145-151).  One kernel (plus
+ * a small memset of arrival counters when the tail is split).
  */
 int b200_joint_attention(const void* q_rot, const void* k_rot, const void* v,
                          const void* prefix_k, const void* prefix_v, int32_t batch,
                          int32_t heads, int32_t target_len, int32_t prefix_len,
                          int32_t head_dim, const b200_kv_desc* desc, float scale, void* out,
-                         int32_t* status, b200_stream_t stream);
+                         void* workspace, size_t workspace_bytes, int32_t* status,
+                         b200_stream_t stream);
 
 /*
  * Plain attention on [B,H,S,D] tensors: out = softmax(q k^T * scale [masked]) v.

@@ -77,7 +77,7 @@ def lib() -> ctypes.CDLL:
         L.b200_norm_rope.argtypes = [vp, vp, i32, i32, i32, i32, vp, f32, vp, vp]
         L.b200_qk_norm_rope.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, vp, vp, f32, vp, vp]
         L.b200_joint_attention.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, f32, vp,
-                                           vp, vp]
+                                           vp, ctypes.c_size_t, vp, vp]
         L.b200_joint_layout.argtypes = [i32, vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]
         L.b200_rope_positions.argtypes = [vp, i32, vp, i32, vp]
         L.b200_rope_pe.argtypes = [vp, i32, vp, i32, vp, f32, vp]
@@ -276,17 +276,23 @@ def qk_norm_rope(q, k, norm_q_w, norm_k_w, eps: float, pe, q_rot=None, k_rot=Non
     return q_rot, k_rot
 
 
+SPLIT_WORKSPACE_BYTES = 21299968  # B200_ATTN_SPLIT_WORKSPACE_BYTES
+
+
 def joint_attention(q_rot, k_rot, v, prefix_k, prefix_v, desc=None, scale=None, out=None,
-                    status=None, stream=None):
+                    workspace=None, status=None, stream=None):
     """The attention launch of b200_attn_fwd: post-RoPE q_rot/k_rot bf16 [B,H,T,D], v bf16
-    [B,T,H,D], prefix bf16 [B,H,P,D] or None -> out bf16 [B,T,H*D]."""
+    [B,T,H,D], prefix bf16 [B,H,P,D] or None -> out bf16 [B,T,H*D].  A uint8 device
+    ``workspace`` of SPLIT_WORKSPACE_BYTES enables the tail split (None: no split)."""
     import torch
     b, h, t, d = q_rot.shape
     p = 0 if prefix_k is None else prefix_k.shape[2]
     if out is None:
         out = torch.empty((b, t, h * d), dtype=torch.bfloat16, device=q_rot.device)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     _check(lib().b200_joint_attention(_dptr(q_rot), _dptr(k_rot), _dptr(v), _dptr(prefix_k),
                                       _dptr(prefix_v), b, h, t, p, d, _dptr(desc),
                                       float(d ** -0.5 if scale is None else scale), _dptr(out),
-                                      _dptr(status), _stream(stream)), "b200_joint_attention")
+                                      _dptr(workspace), ws_bytes, _dptr(status), _stream(stream)),
+           "b200_joint_attention")
     return out

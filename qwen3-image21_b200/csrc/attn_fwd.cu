@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -56,6 +57,17 @@ struct AttnParams {
   __nv_bfloat16* out;
   int64_t out_sb, out_sh, out_sr;  // element strides: batch, head, query row
   int32_t* status;
+  // Work units.  An item is one (batch, head, 256-row query block); items are numbered
+  // with the query block fastest.  Units [0, n_full) are whole items; each of the last
+  // (grid - n_full) / split items is cut into `split` contiguous ranges of key tiles,
+  // one unit each, so the last partial wave of CTAs is spread over more SMs.
+  int32_t H;
+  int32_t nqb;        // query blocks per (batch, head)
+  int32_t n_full;
+  int32_t split;      // 1 = no split units
+  float* part_o;      // [split item][piece][256][128] unnormalised O of each piece
+  float* part_ml;     // [split item][piece][2][256] running max m and sum l per row
+  int32_t* part_cnt;  // [split item] pieces finished; zero before the launch
 };
 
 __device__ __forceinline__ void record_error(const AttnParams& p, volatile int* abort_flag,
@@ -73,6 +85,10 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // ---- packed f32x2 arithmetic (sm_100 FFMA2 / FADD2: two lanes per instruction)
@@ -220,9 +236,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  const int q0 = blockIdx.x * (kQTiles * kBM);
+  const int unit = blockIdx.x;
+  int item = unit, piece = 0;
+  const bool split_unit = unit >= p.n_full;
+  if (split_unit) {
+    item = p.n_full + (unit - p.n_full) / p.split;
+    piece = (unit - p.n_full) % p.split;
+  }
+  const int h = (item / p.nqb) % p.H;
+  const int b = item / (p.nqb * p.H);
+  const int q0 = (item % p.nqb) * (kQTiles * kBM);
 
   // Key tiles: segment 0 (prefix) then segment 1; each segment's last tile may be ragged.
   int pv = 0;
@@ -230,7 +253,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tv = p.seg1_len ? min(max(p.seg1_len[(int64_t)b * p.seg1_stride], 0), p.L1) : p.L1;
   const int n0 = (pv + kBN - 1) / kBN;
   const int n1 = (tv + kBN - 1) / kBN;
-  const int n = n0 + n1;
+  // This unit's key tiles [jb, jb + n) of the n0 + n1 tiles of the item.
+  int jb = 0, n = n0 + n1;
+  if (split_unit) {
+    const int all = n;
+    jb = static_cast<int>(static_cast<int64_t>(all) * piece / p.split);
+    n = static_cast<int>(static_cast<int64_t>(all) * (piece + 1) / p.split) - jb;
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -282,8 +311,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < n && ok; ++j) {
         const int s = j & 1;
         const uint32_t u = static_cast<uint32_t>(j >> 1);
-        const bool seg0 = j < n0;
-        const int row = (seg0 ? j : j - n0) * kBN;
+        const int ja = jb + j;  // tile index within the item
+        const bool seg0 = ja < n0;
+        const int row = (seg0 ? ja : ja - n0) * kBN;
         if (j >= kStages && !wait_or_abort(k_empty + s, (u - 1) & 1, abort_flag)) {
           ok = false;
           break;
@@ -427,7 +457,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int valid = j < n0 ? min(kBN, pv - j * kBN) : min(kBN, tv - (j - n0) * kBN);
+      const int ja = jb + j;
+      const int valid = ja < n0 ? min(kBN, pv - ja * kBN) : min(kBN, tv - (ja - n0) * kBN);
       const float alpha = valid < kBN ? softmax_row<true>(valid, c, m, l, tS)
                                       : softmax_row<false>(valid, c, m, l, tS);
       // O rescale: PV of the previous tile is complete (s_full is committed after it).
@@ -451,29 +482,118 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int qrow = q0 + t * kBM + row;
     const bool store = qrow < p.T;
     __nv_bfloat16* dst = p.out + b * p.out_sb + h * p.out_sh + static_cast<int64_t>(qrow) * p.out_sr;
-    if (n == 0) {
-      // No valid key: the reference's softmax over an all -inf row is NaN.
-      if (store) {
-        const uint4 nan4 = make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
-        for (int i = 0; i < kD / 8; ++i) reinterpret_cast<uint4*>(dst)[i] = nan4;
+    if (!split_unit) {
+      if (n == 0) {
+        // No valid key: the reference's softmax over an all -inf row is NaN.
+        if (store) {
+          const uint4 nan4 = make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
+          for (int i = 0; i < kD / 8; ++i) reinterpret_cast<uint4*>(dst)[i] = nan4;
+        }
+      } else if (ok) {
+        if (!wait_or_abort(o_full + t, 0, abort_flag)) {
+          record_error(p, abort_flag, 4);
+        } else {
+          tc_fence_after();
+          const float inv_l = 1.f / l;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t o[32];
+            tmem_ld32(tO + q * 32, o);
+            tmem_wait_ld();
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              w[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv_l,
+                                 __uint_as_float(o[2 * i + 1]) * inv_l);
+            if (store) {
+              uint4* d4 = reinterpret_cast<uint4*>(dst + q * 32);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            }
+          }
+        }
       }
-    } else if (ok) {
-      if (!wait_or_abort(o_full + t, 0, abort_flag)) {
+    } else {
+      // Split unit: publish this piece's unnormalised O and (m, l); the last piece of the
+      // item to finish merges all pieces (no CTA ever waits for another one).  Both named
+      // barriers are reached by all 256 softmax threads on every path.
+      const int sitem = item - p.n_full;
+      const int slot = sitem * p.split + piece;
+      const int prow = t * kBM + row;  // row within the 256-row block
+      float* po = p.part_o + (static_cast<size_t>(slot) * (kQTiles * kBM) + prow) * kD;
+      bool have = ok && n > 0;
+      if (have && !wait_or_abort(o_full + t, 0, abort_flag)) {
         record_error(p, abort_flag, 4);
-      } else {
+        have = false;
+      }
+      have = __all_sync(0xffffffffu, have);
+      if (have) {
         tc_fence_after();
-        const float inv_l = 1.f / l;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint32_t o[32];
           tmem_ld32(tO + q * 32, o);
           tmem_wait_ld();
-          uint32_t w[16];
+          float4* d4 = reinterpret_cast<float4*>(po + q * 32);
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            w[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv_l,
-                               __uint_as_float(o[2 * i + 1]) * inv_l);
+          for (int i = 0; i < 8; ++i)
+            d4[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
+        }
+      } else {
+        for (int i = 0; i < kD / 4; ++i) reinterpret_cast<float4*>(po)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      float* pml = p.part_ml + static_cast<size_t>(slot) * 2 * (kQTiles * kBM);
+      pml[prow] = have ? m : -INFINITY;
+      pml[kQTiles * kBM + prow] = have ? l : 0.f;
+      __threadfence();
+      named_barrier_sync(1, kQTiles * kBM);
+      volatile int* last_flag = abort_flag + 1;
+      if (threadIdx.x == 4 * 32) {
+        const int done = atomicAdd(p.part_cnt + sitem, 1);
+        const int last = done == p.split - 1;
+        if (last) p.part_cnt[sitem] = 0;  // ready for the next launch
+        *last_flag = last;
+      }
+      named_barrier_sync(1, kQTiles * kBM);
+      if (*last_flag) {
+        __threadfence();
+        const float* ml0 = p.part_ml + static_cast<size_t>(sitem) * p.split * 2 * (kQTiles * kBM);
+        float mmax = -INFINITY;
+        for (int k = 0; k < p.split; ++k)
+          mmax = fmaxf(mmax, __ldcg(ml0 + static_cast<size_t>(k) * 2 * (kQTiles * kBM) + prow));
+        float lsum = 0.f;
+        float wk[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int k = 0; k < p.split && k < 4; ++k) {
+          const float* ml = ml0 + static_cast<size_t>(k) * 2 * (kQTiles * kBM);
+          const float mk = __ldcg(ml + prow);
+          wk[k] = mk == -INFINITY ? 0.f : ex2_approx(mk - mmax);
+          lsum += wk[k] * __ldcg(ml + kQTiles * kBM + prow);
+        }
+        const float inv_l = 1.f / lsum;  // 0/0 = NaN when no piece saw a valid key
+        const float* pbase = p.part_o + (static_cast<size_t>(sitem) * p.split * (kQTiles * kBM) + prow) * kD;
+#pragma unroll 1
+        for (int q = 0; q < 4; ++q) {
+          float acc[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+          for (int k = 0; k < p.split && k < 4; ++k) {
+            const float4* src = reinterpret_cast<const float4*>(
+                pbase + static_cast<size_t>(k) * (kQTiles * kBM) * kD + q * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 x = __ldcg(src + i);
+              acc[4 * i] += wk[k] * x.x;
+              acc[4 * i + 1] += wk[k] * x.y;
+              acc[4 * i + 2] += wk[k] * x.z;
+              acc[4 * i + 3] += wk[k] * x.w;
+            }
+          }
           if (store) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(acc[2 * i] * inv_l, acc[2 * i + 1] * inv_l);
             uint4* d4 = reinterpret_cast<uint4*>(dst + q * 32);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
@@ -517,7 +637,12 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
 __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeJob j0, NormRopeJob j1,
                                                          NormRopeJob j2, int B, int T, int H,
                                                          float eps, const float* pe,
-                                                         int rope_mask) {
+                                                         int rope_mask, int32_t* zero,
+                                                         int n_zero) {
+  // Also clears the attention kernel's split arrival counters (n_zero <= 256), which saves
+  // a separate memset before the attention launch that follows on the same stream.
+  if (zero && blockIdx.x == 0 && blockIdx.y == 0 && static_cast<int>(threadIdx.x) < n_zero)
+    zero[threadIdx.x] = 0;
   // Host guarantees B * T * H < 2^31, so row indices fit 32 bits.
   const NormRopeJob job = blockIdx.y == 0 ? j0 : (blockIdx.y == 1 ? j1 : j2);
   const bool rope = pe != nullptr && ((rope_mask >> blockIdx.y) & 1);
@@ -655,20 +780,77 @@ int ensure_kernel_attrs() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+constexpr size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Tail split.  With `items` work items on `sms` SMs, the last wave holds items % sms
+// CTAs; when that is at most half the SMs, those items are cut into `split` pieces of
+// key tiles (at most 4, and at least 2 tiles a piece for the longest item) so the wave
+// spreads over the idle SMs.  Each piece needs one slot of partial results.
+constexpr int kMaxSplitSlots = 160;  // >= the SM count of sm_100 parts
+constexpr size_t kSplitSlotBytes = size_t{kQTiles} * kBM * kD * 4 + 2 * size_t{kQTiles} * kBM * 4;
+constexpr size_t kSplitRegionBytes =
+    round_up(size_t{kMaxSplitSlots} * kSplitSlotBytes + size_t{kMaxSplitSlots} * 4, 256);
+static_assert(kSplitRegionBytes == B200_ATTN_SPLIT_WORKSPACE_BYTES,
+              "header constant must match the split-region layout");
+
+struct SplitPlan {
+  int n_full, split, units;
+};
+
+int sm_count() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    return 148;
+  return sms;
+}
+
+SplitPlan plan_units(int items, int max_tiles, bool have_region) {
+  SplitPlan sp{items, 1, items};
+  const int sms = sm_count();
+  if (!have_region || items <= sms) return sp;
+  const int tail = items % sms;
+  if (tail == 0 || 2 * tail > sms) return sp;
+  int split = std::min(4, sms / tail);
+  split = std::min(split, max_tiles / 2);
+  split = std::min(split, kMaxSplitSlots / tail);
+  if (split < 2) return sp;
+  sp.n_full = items - tail;
+  sp.split = split;
+  sp.units = sp.n_full + tail * split;
+  return sp;
+}
+
+// Fills the work-unit fields of prm (split region optional) and launches.
 int launch_attention(const CUtensorMap& mq, const CUtensorMap& mk0, const CUtensorMap& mv0,
-                     const CUtensorMap& mk1, const CUtensorMap& mv1, const AttnParams& prm,
-                     int B, int H, int T, cudaStream_t stream) {
+                     const CUtensorMap& mk1, const CUtensorMap& mv1, AttnParams prm, int B,
+                     int H, int T, int max_tiles, void* split_region, cudaStream_t stream,
+                     bool counters_zeroed = false) {
   int rc = ensure_kernel_attrs();
   if (rc != B200_OK) return rc;
-  dim3 grid((T + kQTiles * kBM - 1) / (kQTiles * kBM), H, B);
-  joint_attn_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk0, mv0, mk1, mv1, prm);
+  prm.H = H;
+  prm.nqb = (T + kQTiles * kBM - 1) / (kQTiles * kBM);
+  const int64_t items = static_cast<int64_t>(B) * H * prm.nqb;
+  if (items > 0x7fffffff / 4) return B200_ERR_INVALID;
+  const SplitPlan sp = plan_units(static_cast<int>(items), max_tiles, split_region != nullptr);
+  prm.n_full = sp.n_full;
+  prm.split = sp.split;
+  if (sp.split > 1) {
+    auto* base = static_cast<uint8_t*>(split_region);
+    prm.part_o = reinterpret_cast<float*>(base);
+    prm.part_ml = reinterpret_cast<float*>(base + size_t{kMaxSplitSlots} * kQTiles * kBM * kD * 4);
+    prm.part_cnt = reinterpret_cast<int32_t*>(base + size_t{kMaxSplitSlots} * kSplitSlotBytes);
+    const size_t cnt_bytes = sizeof(int32_t) * static_cast<size_t>(sp.units - sp.n_full) / sp.split;
+    if (!counters_zeroed && cudaMemsetAsync(prm.part_cnt, 0, cnt_bytes, stream) != cudaSuccess)
+      return B200_ERR_CUDA;
+  }
+  joint_attn_kernel<<<dim3(sp.units), kThreads, kSmemBytes, stream>>>(mq, mk0, mv0, mk1, mv1, prm);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
 int launch_norm_rope(const NormRopeJob* jobs, int njobs, int B, int T, int H, float eps,
-                     const float* pe, int rope_mask, cudaStream_t stream) {
+                     const float* pe, int rope_mask, cudaStream_t stream,
+                     int32_t* zero = nullptr, int n_zero = 0) {
   const int64_t rows = static_cast<int64_t>(B) * T * H;
   if (rows == 0 || njobs == 0) return B200_OK;
   if (rows >= (int64_t{1} << 31)) return B200_ERR_INVALID;
@@ -677,7 +859,8 @@ int launch_norm_rope(const NormRopeJob* jobs, int njobs, int B, int T, int H, fl
   if (blocks > 0x7fffffff) return B200_ERR_INVALID;
   NormRopeJob j[3] = {jobs[0], njobs > 1 ? jobs[1] : jobs[0], njobs > 2 ? jobs[2] : jobs[0]};
   dim3 grid(static_cast<unsigned>(blocks), njobs);
-  norm_rope_kernel<<<grid, 256, 0, stream>>>(j[0], j[1], j[2], B, T, H, eps, pe, rope_mask);
+  norm_rope_kernel<<<grid, 256, 0, stream>>>(j[0], j[1], j[2], B, T, H, eps, pe, rope_mask, zero,
+                                             n_zero);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
@@ -685,7 +868,8 @@ int launch_norm_rope(const NormRopeJob* jobs, int njobs, int B, int T, int H, fl
 // v (B,T,H,D, token-major)], out [B,T,H*D].  Arguments are already validated.
 int joint_attention(const void* q_rot, const void* k_rot, const void* v, const void* prefix_k,
                     const void* prefix_v, int B, int H, int T, int P, const b200_kv_desc* desc,
-                    float scale, void* out, int32_t* status, cudaStream_t stream) {
+                    float scale, void* out, int32_t* status, void* split_region,
+                    cudaStream_t stream, bool counters_zeroed = false) {
   CUtensorMap mq{}, mk0{}, mv0{}, mk1{}, mv1{};
   int rc;
   if ((rc = make_map(&mq, q_rot, B, H, T, true)) != B200_OK) return rc;
@@ -710,7 +894,9 @@ int joint_attention(const void* q_rot, const void* k_rot, const void* v, const v
   prm.out_sh = kD;
   prm.out_sr = static_cast<int64_t>(H) * kD;
   prm.status = status;
-  return launch_attention(mq, mk0, mv0, mk1, mv1, prm, B, H, T, stream);
+  const int max_tiles = (P + kBN - 1) / kBN + (T + kBN - 1) / kBN;
+  return launch_attention(mq, mk0, mv0, mk1, mv1, prm, B, H, T, max_tiles, split_region, stream,
+                          counters_zeroed);
 }
 
 }  // namespace
@@ -724,7 +910,7 @@ extern "C" int b200_attn_workspace_bytes(const b200_attn_args* a, size_t* bytes)
   const size_t tensor = static_cast<size_t>(a->batch) * a->heads * a->target_len * kD * 2;
   size_t need = round_up(tensor, 256);               // post-RoPE Q
   if (!a->k_rot_out) need += round_up(tensor, 256);  // post-RoPE K
-  *bytes = need;
+  *bytes = need + kSplitRegionBytes;                 // partial results of the tail split
   return B200_OK;
 }
 
@@ -745,7 +931,8 @@ extern "C" int b200_attn_fwd(const b200_attn_args* a, b200_stream_t stream_) {
     if (ptr && !aligned16(ptr)) return B200_ERR_INVALID;
   size_t need = 0;
   b200_attn_workspace_bytes(a, &need);
-  if (!a->workspace || a->workspace_bytes < need) return B200_ERR_WORKSPACE;
+  const size_t need_min = need - kSplitRegionBytes;  // without the tail split
+  if (!a->workspace || a->workspace_bytes < need_min) return B200_ERR_WORKSPACE;
 
   const int B = a->batch, H = a->heads, T = a->target_len, P = a->prefix_len;
   const size_t tensor = static_cast<size_t>(B) * H * T * kD * 2;
@@ -758,18 +945,25 @@ extern "C" int b200_attn_fwd(const b200_attn_args* a, b200_stream_t stream_) {
       {static_cast<const __nv_bfloat16*>(a->q), q_rot, a->norm_q_w},
       {static_cast<const __nv_bfloat16*>(a->k), k_rot, a->norm_k_w},
       {static_cast<const __nv_bfloat16*>(a->v), static_cast<__nv_bfloat16*>(a->v_out), nullptr}};
-  int rc = launch_norm_rope(jobs, a->v_out ? 3 : 2, B, T, H, a->norm_eps, a->pe, 0x3, stream);
+  void* split_region = a->workspace_bytes >= need ? ws + need_min : nullptr;
+  int32_t* counters = split_region
+                          ? reinterpret_cast<int32_t*>(static_cast<uint8_t*>(split_region) +
+                                                       size_t{kMaxSplitSlots} * kSplitSlotBytes)
+                          : nullptr;
+  int rc = launch_norm_rope(jobs, a->v_out ? 3 : 2, B, T, H, a->norm_eps, a->pe, 0x3, stream,
+                            counters, counters ? kMaxSplitSlots : 0);
   if (rc != B200_OK) return rc;
 
   return joint_attention(q_rot, k_rot, a->v, a->prefix_k, a->prefix_v, B, H, T, P, a->desc,
-                         a->scale, a->out, a->status, stream);
+                         a->scale, a->out, a->status, split_region, stream, true);
 }
 
 extern "C" int b200_joint_attention(const void* q_rot, const void* k_rot, const void* v,
                                     const void* prefix_k, const void* prefix_v, int32_t batch,
                                     int32_t heads, int32_t target_len, int32_t prefix_len,
                                     int32_t head_dim, const b200_kv_desc* desc, float scale,
-                                    void* out, int32_t* status, b200_stream_t stream) {
+                                    void* out, void* workspace, size_t workspace_bytes,
+                                    int32_t* status, b200_stream_t stream) {
   if (head_dim != kD) return B200_ERR_UNSUPPORTED;
   if (batch <= 0 || heads <= 0 || target_len < 0 || prefix_len < 0) return B200_ERR_INVALID;
   if (target_len == 0) return B200_OK;
@@ -779,8 +973,11 @@ extern "C" int b200_joint_attention(const void* q_rot, const void* k_rot, const 
   for (const void* ptr : ptrs)
     if (ptr && !aligned16(ptr)) return B200_ERR_INVALID;
   if (!(scale > 0.f) || !std::isfinite(scale)) return B200_ERR_INVALID;
+  if (workspace && !aligned16(workspace)) return B200_ERR_INVALID;
+  void* split_region = workspace && workspace_bytes >= kSplitRegionBytes ? workspace : nullptr;
   return joint_attention(q_rot, k_rot, v, prefix_k, prefix_v, batch, heads, target_len,
-                         prefix_len, desc, scale, out, status, static_cast<cudaStream_t>(stream));
+                         prefix_len, desc, scale, out, status, split_region,
+                         static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int b200_chunked_attention(const void* q, const void* k, const void* v, void* out,
@@ -811,8 +1008,8 @@ extern "C" int b200_chunked_attention(const void* q, const void* k, const void* 
   prm.out_sh = static_cast<int64_t>(sq) * kD;
   prm.out_sr = kD;
   prm.status = status;
-  return launch_attention(mq, mk0, mv0, mk1, mv1, prm, batch, heads, sq,
-                          static_cast<cudaStream_t>(stream_));
+  return launch_attention(mq, mk0, mv0, mk1, mv1, prm, batch, heads, sq, (skv + kBN - 1) / kBN,
+                          nullptr, static_cast<cudaStream_t>(stream_));
 }
 
 extern "C" int b200_norm_rope(const void* x, void* y, int32_t batch, int32_t tokens,
@@ -862,7 +1059,10 @@ extern "C" int b200_attn_fwd_noalloc(const b200_attn_args* args, b200_stream_t s
   size_t need = 0;
   int rc = b200_attn_workspace_bytes(args, &need);
   if (rc != B200_OK) return rc;
-  if (need > B200_NOALLOC_SCRATCH_BYTES) return B200_ERR_WORKSPACE;  // over the fixed limit
+  // The limit applies to the required scratch; the optional tail-split region is used
+  // only when it also fits (b200_attn_fwd decides from workspace_bytes).
+  if (need - B200_ATTN_SPLIT_WORKSPACE_BYTES > B200_NOALLOC_SCRATCH_BYTES)
+    return B200_ERR_WORKSPACE;  // over the fixed limit
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return B200_ERR_CUDA;
   if (dev < 0 || dev >= 64) return B200_ERR_UNSUPPORTED;

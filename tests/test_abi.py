@@ -130,6 +130,10 @@ def test_workspace_bytes():
     a = b200attn.AttnArgs()
     a.batch, a.heads, a.head_dim, a.target_len = 1, 32, 128, 4096
     n = b200attn.workspace_bytes(a)
-    assert n == 2 * 32 * 4096 * 128 * 2
+    split = b200attn.SPLIT_WORKSPACE_BYTES
+    assert n == 2 * 32 * 4096 * 128 * 2 + split
     a.k_rot_out = 256
-    assert b200attn.workspace_bytes(a) == 32 * 4096 * 128 * 2
+    assert b200attn.workspace_bytes(a) == 32 * 4096 * 128 * 2 + split
+    # the header constant matches the binding's
+    hdr = open(os.path.join(ROOT, "include", "b200_attn.h")).read()
+    assert f"B200_ATTN_SPLIT_WORKSPACE_BYTES {split}u" in hdr

@@ -246,3 +246,43 @@ def test_full_size_configs(cuda, T, P, pv):
     out3 = run_gpu(d3)
     torch.cuda.synchronize()
     assert float((out3.float() - 0.75).abs().max()) < 4e-3
+
+
+# ------------------------------------------------------------------ tail split
+def _check_heads(out, h, heads):
+    """Oracle on a subset of heads (heads are independent)."""
+    sub = dict(h)
+    for key in ("q", "k", "v"):
+        sub[key] = h[key][:, :, heads]
+    for key in ("pk", "pv"):
+        sub[key] = None if h[key] is None else h[key][:, heads]
+    want, _, _ = run_oracle(sub)
+    b, t = want.shape[:2]
+    got = f32np(out).reshape(b, t, -1, 128)[:, :, heads].reshape(b, t, -1)
+    check(got, want)
+
+
+@pytest.mark.parametrize("T,P,pv,extra", [
+    (512, 512, None, 3),     # 2 query blocks per head; last wave of 3-4 items split 4 ways
+    (256, 512, [0], 2),      # 2 key tiles cut into 3 pieces: one piece has no tile
+    (512, 300, [263], 5),    # ragged prefix inside split pieces
+])
+def test_tail_split_matches_oracle(cuda, T, P, pv, extra):
+    torch = _torch()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    nqb = (T + 255) // 256
+    H = (sms + extra + nqb - 1) // nqb  # items = H * nqb lands just past a full wave
+    d, h = make_case(1, T, H, P, 3000 + T + P + extra, cuda, pv=pv)
+    ws = torch.empty(b200attn.SPLIT_WORKSPACE_BYTES, dtype=torch.uint8, device=cuda)
+    q_rot, k_rot = b200attn.qk_norm_rope(d["q"], d["k"], d["wq"], d["wk"], 1e-6, d["pe"])
+    out_split = b200attn.joint_attention(q_rot, k_rot, d["v"], d["pk"], d["pv"], desc=d["desc"],
+                                         workspace=ws)
+    out_again = b200attn.joint_attention(q_rot, k_rot, d["v"], d["pk"], d["pv"], desc=d["desc"],
+                                         workspace=ws)
+    out_plain = b200attn.joint_attention(q_rot, k_rot, d["v"], d["pk"], d["pv"], desc=d["desc"])
+    out_fwd = run_gpu(d)  # b200_attn_fwd with its full workspace (split region included)
+    torch.cuda.synchronize()
+    assert torch.equal(out_split, out_again)  # arrival counters reset themselves
+    assert torch.equal(out_fwd, out_split)
+    check(f32np(out_split), f32np(out_plain), rel=2e-3, mx=1e-2)  # merge vs single pass
+    _check_heads(out_split, h, [0, H - 3, H - 2, H - 1])  # the last items are the split ones
