@@ -38,6 +38,9 @@ CONFIGS = {
     # plus 2432 other prompt tokens: a 10624-token prefix with its last 37 keys padded
     "c3": dict(grid=(64, 64), P=10624, pv=10587, layers=32, cond=[(64, 64), (64, 64)],
                name="1024^2 edit, 2 refs (config 3)"),
+    # 2048^2: heads sharded 32/N per GPU, to_out partial sums all-reduced (one block per step)
+    "c4": dict(grid=(128, 128), P=512, pv=None, layers=1, cond=[], hidden=4096,
+               name="2048^2 T2I, head-sharded (config 4)"),
 }
 
 
@@ -243,6 +246,7 @@ def main():
     import torch.distributed as dist
 
     import b200attn
+    from b200attn import dist as bdist
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -250,6 +254,9 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     cfg = CONFIGS[args.config]
+    if args.config == "c4":
+        run_head_sharded(args, cfg, rank, world, dev)
+        return
     gh, gw = cfg["grid"]
     T, P, L = gh * gw, cfg["P"], args.layers or cfg["layers"]
 
@@ -386,6 +393,94 @@ def main():
                 "path": "b200_attn_fwd with pinned-host q/k/v in and output out per block"},
             "clocks": clocks.summary(),
             "gpu_launches": args.steps * L * 2,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_head_sharded(args, cfg, rank, world, dev):
+    """Config 4: each rank runs the attention of its 32/N heads, its share of to_out, and
+    one NCCL all-reduce of the partial sums; a step is one block (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+
+    import b200attn
+    from b200attn import dist as bdist
+
+    gh, gw = cfg["grid"]
+    T, P, hidden = gh * gw, cfg["P"], cfg["hidden"]
+    h0, h1 = bdist.head_shard(HEADS, world, rank)
+    hl = h1 - h0
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    randn = lambda *shape: torch.randn(*shape, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    q, k, v = randn(1, T, hl, HEAD_DIM), randn(1, T, hl, HEAD_DIM), randn(1, T, hl, HEAD_DIM)
+    pk, pv = randn(1, hl, P, HEAD_DIM), randn(1, hl, P, HEAD_DIM)
+    gw_ = torch.Generator(device=dev).manual_seed(99)  # to_out weights identical on every rank
+    w_out = (0.02 * torch.randn(hidden, HEADS * HEAD_DIM, generator=gw_, device=dev)).to(torch.bfloat16)
+    lay = b200attn.joint_layout(P, None, [], (gh, gw))
+    pe = torch.from_numpy(b200attn.rope_pe(lay["img_shapes"], lay["image_pad_mask"])[P:]).to(dev)
+    ones = torch.ones(HEAD_DIM, device=dev, dtype=torch.float32)
+    q_rot = torch.empty(1, hl, T, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    k_rot = torch.empty_like(q_rot)
+    attn = torch.empty(1, T, hl * HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    split_ws = torch.empty(b200attn.SPLIT_WORKSPACE_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(mark=None):
+        b200attn.qk_norm_rope(q, k, ones, ones, 1e-6, pe, q_rot, k_rot, stream=stream)
+        if mark is not None:
+            mark[0].record(stream)
+        b200attn.joint_attention(q_rot, k_rot, v, pk, pv, out=attn, workspace=split_ws,
+                                 stream=stream)
+        if mark is not None:
+            mark[1].record(stream)
+        part = bdist.out_proj_partial(attn.view(T, hl * HEAD_DIM), w_out, h0, h1, HEAD_DIM)
+        bdist.allreduce_sum_(part)
+        return part
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    with ClockSampler(uuid) as clocks:
+        barrier()
+        e0.record(stream)
+        for s_ in range(args.steps):
+            step(marks[s_])
+        e1.record(stream)
+        barrier()
+    ms_step = bdist.max_over_ranks(e0.elapsed_time(e1) / args.steps, device=dev)
+    attn_ms = bdist.max_over_ranks(sum(m[0].elapsed_time(m[1]) for m in marks) / args.steps, device=dev)
+    attn_flops = 4.0 * HEADS * T * (P + T) * HEAD_DIM
+    proj_flops = 2.0 * T * HEADS * HEAD_DIM * hidden
+    if rank == 0:
+        pk_d, src = peaks()
+        peak = float(pk_d.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+        achieved = attn_flops * hl / HEADS / (attn_ms / 1e3) / 1e12
+        line = {
+            "metric": "block TFLOP/s at 2048^2, head-sharded (attention + to_out + all-reduce)",
+            "value": (attn_flops + proj_flops) / (ms_step / 1e3) / 1e12, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) q/k/v and prefix cache, N(0,0.02) to_out)",
+            "config": {"workload": cfg["name"] + ", one block per step", "T": T, "P": P,
+                       "heads_per_gpu": hl, "head_dim": HEAD_DIM, "hidden": hidden,
+                       "parallelism": f"heads/{world} + NCCL all-reduce of to_out partials",
+                       "l2": "inputs exceed L2"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None, "kernel": "joint_attn_kernel",
+                         "peak_source": f"{src} bf16_tflops_sustained", "launch_ms": attn_ms},
+            "cpu_baseline": None, "e2e": None, "clocks": clocks.summary(),
+            "gpu_launches": args.steps * 2,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -1,0 +1,75 @@
+"""Head-sharded joint attention over 2 GPUs (NCCL): each rank runs the CUDA kernel on its
+heads and its share of to_out, the partial sums are all-reduced, and the result must match
+the single-GPU layer (all heads, full to_out).  Skipped with fewer than 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs(T, P, H, hidden):
+    import torch
+    g = torch.Generator().manual_seed(7)
+    bf = lambda *s: torch.randn(*s, generator=g).to(torch.bfloat16)
+    return dict(q=bf(1, T, H, 128), k=bf(1, T, H, 128), v=bf(1, T, H, 128),
+                pk=bf(1, H, P, 128), pv=bf(1, H, P, 128),
+                w_out=(0.02 * torch.randn(hidden, H * 128, generator=g)).to(torch.bfloat16))
+
+
+def _rank(rank, world, port, result_path):
+    import torch
+    import torch.distributed as dist
+
+    import b200attn
+    from b200attn import dist as bdist
+    from oracle import reference as ref
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, device_id=dev)
+    try:
+        T, P, H, hidden = 512, 256, 8, 1024
+        x = {k: v.to(dev) for k, v in _inputs(T, P, H, hidden).items()}
+        lay = ref.joint_layout(P, None, [], (16, 32))
+        pe = torch.from_numpy(ref.embed_nd(lay["img_shapes"], lay["image_pad_mask"])[P:]).to(dev)
+        w = torch.ones(128, device=dev)
+        h0, h1 = bdist.head_shard(H, world, rank)
+        out = bdist.head_sharded_attention_layer(
+            x["q"][:, :, h0:h1].contiguous(), x["k"][:, :, h0:h1].contiguous(),
+            x["v"][:, :, h0:h1].contiguous(), x["pk"][:, h0:h1].contiguous(),
+            x["pv"][:, h0:h1].contiguous(), w, w, pe, x["w_out"], h0, h1)
+        torch.cuda.synchronize()
+        if rank == 0:
+            full = b200attn.attention_forward(x["q"], x["k"], x["v"], x["pk"], x["pv"], w, w, pe)
+            want = torch.matmul(full.view(T, H * 128), x["w_out"].t()).view(1, T, hidden)
+            torch.cuda.synchronize()
+            a = out.float().cpu().numpy()
+            b = want.float().cpu().numpy()
+            rel = float(np.linalg.norm(a - b) / np.linalg.norm(b))
+            with open(result_path, "w") as f:
+                f.write(str(rel))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_head_sharded_layer_matches_single_gpu(tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    result = tmp_path / "rel.txt"
+    mp.spawn(_rank, args=(2, _free_port(), str(result)), nprocs=2, join=True)
+    rel = float(result.read_text())
+    assert rel <= 5e-3, rel
