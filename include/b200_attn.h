@@ -30,7 +30,7 @@ extern "C" {
 #endif
 
 #define B200_ATTN_HEAD_DIM 128
-#define B200_ATTN_ABI_VERSION 1
+#define B200_ATTN_ABI_VERSION 2
 
 typedef enum {
   B200_OK = 0,
@@ -88,6 +88,11 @@ typedef struct {
   size_t workspace_bytes;
   int32_t* status;     /* device int32 or NULL: set non-zero if a device-side wait
                           ran out (1 = load, 2 = mma, 3 = softmax, 4 = epilogue)   */
+  const int32_t* row_limit; /* device [T] or NULL: query row q sees only this call's keys
+                          [0, row_limit[q]) (non-decreasing in q).  The prefix-fill pass
+                          passes b200_block_causal_limits() of its layout with
+                          prefix_len = 0, which replaces build_block_causal_mask
+                          (src/attention_mask.rs:18-66, src/transformer.rs:696-702)  */
 } b200_attn_args;
 
 /*
@@ -225,6 +230,15 @@ int b200_rope_pe(const int32_t* img_shapes, int32_t n_shapes,
  */
 int b200_key_valid_to_desc(const uint8_t* key_valid, int32_t batch, int32_t prefix_len,
                            int32_t target_len, b200_kv_desc* desc_out);
+
+/*
+ * Block-causal mask as per-row key limits (src/attention_mask.rs:18-66): a text token
+ * (image_ids[i] < 0) sees keys [0, i+1); a token of image block k sees keys [0, e) where
+ * e is one past the block's last token (causal OR same image block).  image_ids host
+ * [len] (JointLayout.image_ids, text -1, blocks contiguous); limits_out host [len].
+ * Combine with b200_kv_desc.target_valid for the padded-key part of the mask.
+ */
+int b200_block_causal_limits(const int64_t* image_ids, int32_t len, int32_t* limits_out);
 
 /* Human-readable text of a b200_status. */
 const char* b200_strerror(int status);

@@ -209,6 +209,18 @@ def block_causal_mask(image_ids: Sequence[int], key_valid_: Optional[np.ndarray]
     return np.broadcast_to(allowed, (batch, 1, s, s)).copy()
 
 
+def block_causal_limits_from_mask(mask2d: np.ndarray):
+    """Per-row key limits of a dense [S,S] mask whose rows are leading runs of keys
+    (build_block_causal_mask without key_valid); None if a row is not a leading run."""
+    out = []
+    for row in mask2d.astype(bool):
+        n = int(row.sum())
+        if not row[:n].all():
+            return None
+        out.append(n)
+    return np.asarray(out, np.int32)
+
+
 def key_valid_to_desc(kv: np.ndarray, prefix_len: int, target_len: int):
     """Descriptor form of a cached step's key_valid [B, P+T]: (prefix_valid, target_valid)
     per row; None if padding is not a prefix suffix (then no descriptor exists)."""

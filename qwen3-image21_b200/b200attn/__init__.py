@@ -30,6 +30,7 @@ EXPORTED = (
     "b200_attn_workspace_bytes", "b200_attn_fwd", "b200_joint_attention", "b200_chunked_attention",
     "b200_norm_rope", "b200_qk_norm_rope",
     "b200_joint_layout", "b200_rope_positions", "b200_rope_pe", "b200_key_valid_to_desc",
+    "b200_block_causal_limits",
     "b200_strerror", "b200_abi_version",
 )
 
@@ -57,6 +58,7 @@ class AttnArgs(ctypes.Structure):
         ("scale", ctypes.c_float), ("out", ctypes.c_void_p), ("k_rot_out", ctypes.c_void_p),
         ("v_out", ctypes.c_void_p), ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t), ("status", ctypes.c_void_p),
+        ("row_limit", ctypes.c_void_p),
     ]
 
 
@@ -82,6 +84,7 @@ def lib() -> ctypes.CDLL:
         L.b200_rope_positions.argtypes = [vp, i32, vp, i32, vp]
         L.b200_rope_pe.argtypes = [vp, i32, vp, i32, vp, f32, vp]
         L.b200_key_valid_to_desc.argtypes = [vp, i32, i32, i32, vp]
+        L.b200_block_causal_limits.argtypes = [vp, i32, vp]
         L.b200_strerror.argtypes = [ctypes.c_int]
         L.b200_strerror.restype = ctypes.c_char_p
         for name in EXPORTED:
@@ -146,6 +149,15 @@ def rope_pe(img_shapes, image_pad_mask, axes=(16, 56, 56), theta: float = 1e4) -
     return out
 
 
+def block_causal_limits(image_ids) -> np.ndarray:
+    """Per-row key limits of the block-causal mask (src/attention_mask.rs:18-66)."""
+    ids = np.ascontiguousarray(image_ids, np.int64)
+    out = np.zeros(ids.shape[0], np.int32)
+    _check(lib().b200_block_causal_limits(_np_ptr(ids), ids.shape[0], _np_ptr(out)),
+           "block_causal_limits")
+    return out
+
+
 def key_valid_to_desc(key_valid: np.ndarray, prefix_len: int, target_len: int) -> np.ndarray:
     """[B, P+T] 0/1 mask -> int32 [B, 2] descriptors (prefix_valid, target_valid)."""
     kv = np.ascontiguousarray(key_valid, np.uint8)
@@ -168,7 +180,8 @@ def _dptr(t) -> Optional[int]:
 
 
 def make_args(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w, pe, out, desc=None, scale=None,
-              eps: float = 1e-6, k_rot_out=None, v_out=None, workspace=None, status=None) -> AttnArgs:
+              eps: float = 1e-6, k_rot_out=None, v_out=None, workspace=None, status=None,
+              row_limit=None) -> AttnArgs:
     """Fill b200_attn_args from torch tensors (no checks beyond what the library does)."""
     b, t, h, d = q.shape
     p = 0 if prefix_k is None else prefix_k.shape[2]
@@ -186,6 +199,7 @@ def make_args(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w, pe, out, desc=Non
     a.workspace = _dptr(workspace)
     a.workspace_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     a.status = _dptr(status)
+    a.row_limit = _dptr(row_limit)
     return a
 
 
@@ -197,7 +211,7 @@ def workspace_bytes(args: AttnArgs) -> int:
 
 def attention_forward(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w, pe, desc=None, scale=None,
                       eps: float = 1e-6, out=None, k_rot_out=None, v_out=None, workspace=None,
-                      status=None, stream=None):
+                      status=None, stream=None, row_limit=None):
     """The Attention::forward span from the norm to the head merge on the GPU.
 
     q, k, v: bf16 [B,T,H,D] raw projections; prefix_k/v: bf16 [B,H,P,D] (or None);
@@ -209,7 +223,7 @@ def attention_forward(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w, pe, desc=
     if out is None:
         out = torch.empty((b, t, h * d), dtype=torch.bfloat16, device=q.device)
     args = make_args(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w, pe, out, desc, scale, eps,
-                     k_rot_out, v_out, None, status)
+                     k_rot_out, v_out, None, status, row_limit)
     if workspace is None:
         need = workspace_bytes(args)
         workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)

@@ -53,6 +53,10 @@ struct AttnParams {
   const int32_t* seg0_len;   // valid keys of segment 0 per batch row (stride seg0_stride)
   const int32_t* seg1_len;
   int32_t seg0_stride, seg1_stride;
+  // Optional per-query-row limit on segment-1 keys (keys [0, row_limit[q]) are visible),
+  // shared by all batch rows and non-decreasing in q: the block-causal mask of the
+  // prefix-fill pass.  NULL: every valid key is visible.
+  const int32_t* row_limit;
   float scale_log2;          // scale * log2(e)
   __nv_bfloat16* out;
   int64_t out_sb, out_sh, out_sr;  // element strides: batch, head, query row
@@ -251,8 +255,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   int pv = 0;
   if (p.P > 0) pv = p.seg0_len ? min(max(p.seg0_len[(int64_t)b * p.seg0_stride], 0), p.P) : p.P;
   const int tv = p.seg1_len ? min(max(p.seg1_len[(int64_t)b * p.seg1_stride], 0), p.L1) : p.L1;
+  // With row limits, this block's rows see at most row_limit[last row] keys (the limits
+  // are non-decreasing), so later key tiles are skipped.
+  const int tv_blk =
+      p.row_limit ? min(tv, max(p.row_limit[min(q0 + kQTiles * kBM, p.T) - 1], 0)) : tv;
   const int n0 = (pv + kBN - 1) / kBN;
-  const int n1 = (tv + kBN - 1) / kBN;
+  const int n1 = (tv_blk + kBN - 1) / kBN;
   // This unit's key tiles [jb, jb + n) of the n0 + n1 tiles of the item.
   int jb = 0, n = n0 + n1;
   if (split_unit) {
@@ -451,6 +459,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m = -INFINITY;  // running max, scaled (log2) units
     float l = 0.f;        // running sum of p
     bool ok = true;
+    // This row's visible segment-1 keys (row limit, then the batch row's valid length).
+    const int qrow_lim = q0 + t * kBM + row;
+    const int tv_row =
+        p.row_limit ? min(tv, max(p.row_limit[min(qrow_lim, p.T - 1)], 0)) : tv;
     for (int j = 0; j < n; ++j) {
       if (!wait_or_abort(s_full + t, j & 1, abort_flag)) {
         ok = false;
@@ -458,9 +470,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const int ja = jb + j;
-      const int valid = ja < n0 ? min(kBN, pv - ja * kBN) : min(kBN, tv - (ja - n0) * kBN);
-      const float alpha = valid < kBN ? softmax_row<true>(valid, c, m, l, tS)
-                                      : softmax_row<false>(valid, c, m, l, tS);
+      const int valid = ja < n0 ? min(kBN, pv - ja * kBN) : min(kBN, tv_row - (ja - n0) * kBN);
+      // Rows of a warp may have different limits: any masked lane sends the whole warp down
+      // the masked path (TMEM loads are warp-collective).
+      const float alpha = __any_sync(0xffffffffu, valid < kBN)
+                              ? softmax_row<true>(valid, c, m, l, tS)
+                              : softmax_row<false>(valid, c, m, l, tS);
       // O rescale: PV of the previous tile is complete (s_full is committed after it).
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
@@ -869,7 +884,8 @@ int launch_norm_rope(const NormRopeJob* jobs, int njobs, int B, int T, int H, fl
 int joint_attention(const void* q_rot, const void* k_rot, const void* v, const void* prefix_k,
                     const void* prefix_v, int B, int H, int T, int P, const b200_kv_desc* desc,
                     float scale, void* out, int32_t* status, void* split_region,
-                    cudaStream_t stream, bool counters_zeroed = false) {
+                    cudaStream_t stream, bool counters_zeroed = false,
+                    const int32_t* row_limit = nullptr) {
   CUtensorMap mq{}, mk0{}, mv0{}, mk1{}, mv1{};
   int rc;
   if ((rc = make_map(&mq, q_rot, B, H, T, true)) != B200_OK) return rc;
@@ -886,6 +902,7 @@ int joint_attention(const void* q_rot, const void* k_rot, const void* v, const v
   prm.v1_token_major = 1;
   prm.seg0_len = desc ? &desc[0].prefix_valid : nullptr;
   prm.seg1_len = desc ? &desc[0].target_valid : nullptr;
+  prm.row_limit = row_limit;
   prm.seg0_stride = 2;
   prm.seg1_stride = 2;
   prm.scale_log2 = scale * 1.4426950408889634f;
@@ -955,7 +972,7 @@ extern "C" int b200_attn_fwd(const b200_attn_args* a, b200_stream_t stream_) {
   if (rc != B200_OK) return rc;
 
   return joint_attention(q_rot, k_rot, a->v, a->prefix_k, a->prefix_v, B, H, T, P, a->desc,
-                         a->scale, a->out, a->status, split_region, stream, true);
+                         a->scale, a->out, a->status, split_region, stream, true, a->row_limit);
 }
 
 extern "C" int b200_joint_attention(const void* q_rot, const void* k_rot, const void* v,

@@ -4,6 +4,7 @@
 //   b200_rope_positions     EmbedNd::forward positions  src/rope.rs:118-172
 //   b200_rope_pe            EmbedNd::new + forward      src/rope.rs:37-211
 //   b200_key_valid_to_desc  key_valid (cached step)     src/transformer.rs:642-649, 736-745
+//   b200_block_causal_limits block-causal mask as row limits  src/attention_mask.rs:18-66
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -190,6 +191,24 @@ extern "C" int b200_key_valid_to_desc(const uint8_t* key_valid, int32_t batch,
       if (!row[k]) return B200_ERR_LAYOUT;  // target keys are always valid in the reference
     desc_out[b].prefix_valid = pv;
     desc_out[b].target_valid = target_len;
+  }
+  return B200_OK;
+}
+
+extern "C" int b200_block_causal_limits(const int64_t* image_ids, int32_t len,
+                                        int32_t* limits_out) {
+  if (len < 0 || (len > 0 && (!image_ids || !limits_out))) return B200_ERR_INVALID;
+  int32_t i = 0;
+  while (i < len) {
+    if (image_ids[i] < 0) {  // text: causal
+      limits_out[i] = i + 1;
+      ++i;
+      continue;
+    }
+    int32_t e = i;  // image block [i, e): every token sees the whole block and all before it
+    while (e < len && image_ids[e] == image_ids[i]) ++e;
+    for (int32_t r = i; r < e; ++r) limits_out[r] = e;
+    i = e;
   }
   return B200_OK;
 }

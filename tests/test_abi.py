@@ -29,7 +29,9 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), f"{n} declared in include/b200_attn.h but not exported"
     assert set(names) <= set(b200attn.EXPORTED) | {"b200_attn_fwd_noalloc"}
-    assert lib.b200_abi_version() == 1
+    hdr = open(os.path.join(ROOT, "include", "b200_attn.h")).read()
+    version = int(re.search(r"#define B200_ATTN_ABI_VERSION (\d+)", hdr).group(1))
+    assert lib.b200_abi_version() == version
 
 
 def test_strerror():
@@ -137,3 +139,20 @@ def test_workspace_bytes():
     # the header constant matches the binding's
     hdr = open(os.path.join(ROOT, "include", "b200_attn.h")).read()
     assert f"B200_ATTN_SPLIT_WORKSPACE_BYTES {split}u" in hdr
+
+
+@pytest.mark.parametrize("text,cond", [(3, []), (40, [(4, 6), (8, 8)]), (9, [(2, 2), (2, 2)])])
+def test_block_causal_limits_match_the_reference_mask(text, cond):
+    """b200_block_causal_limits == the leading-run lengths of build_block_causal_mask
+    (src/attention_mask.rs:18-66) over the prefix of the joint layout."""
+    slots = [False] * text
+    p = 1
+    for (h, w) in cond:
+        slots[p:p + h * w // 4] = [True] * (h * w // 4)
+        p += h * w // 4 + 1
+    lay = ref.joint_layout(text, slots, cond, (2, 2))
+    ids = lay["image_ids"]
+    want = ref.block_causal_limits_from_mask(ref.block_causal_mask(ids, None, 1)[0, 0])
+    assert want is not None
+    assert np.array_equal(b200attn.block_causal_limits(ids), want)
+    assert np.all(np.diff(want) >= 0)  # non-decreasing: the kernel relies on it

@@ -286,3 +286,43 @@ def test_tail_split_matches_oracle(cuda, T, P, pv, extra):
     assert torch.equal(out_fwd, out_split)
     check(f32np(out_split), f32np(out_plain), rel=2e-3, mx=1e-2)  # merge vs single pass
     _check_heads(out_split, h, [0, H - 3, H - 2, H - 1])  # the last items are the split ones
+
+
+
+# ------------------------------------------------------------------ prefix fill (block-causal)
+@pytest.mark.parametrize("cond,pad", [([], 0), ([(8, 16), (16, 16)], 7), ([(16, 16)], 0)])
+def test_prefix_fill_block_causal_matches_oracle(cuda, cond, pad):
+    """The prefix-only pass (src/transformer.rs:674-707): the prefix attends to itself under
+    the block-causal mask times key_valid; its post-RoPE K and V fill the cache."""
+    torch = _torch()
+    slots, lead = [], 10
+    for (hh, ww) in cond:
+        slots += [False] * lead + [True] * (hh * ww // 4)
+    slots += [False] * 150
+    lay = ref.joint_layout(len(slots), slots, cond, (2, 2))
+    P, H = lay["prefix_len"], 4
+    ids = lay["image_ids"][:P]
+    limits = b200attn.block_causal_limits(ids)
+    pe = ref.embed_nd(lay["img_shapes"], lay["image_pad_mask"])[:P]
+    g = torch.Generator().manual_seed(P + pad)
+    q, k, v = (bf16(torch.randn(1, P, H, 128, generator=g)) for _ in range(3))
+    w = torch.ones(128)
+    pv = P - pad  # padded prompt tokens sit at the end of the prompt
+    desc = torch.tensor([[0, pv]], dtype=torch.int32, device=cuda) if pad else None
+    k_rot = torch.empty(1, H, P, 128, dtype=torch.bfloat16, device=cuda)
+    v_out = torch.empty(1, H, P, 128, dtype=torch.bfloat16, device=cuda)
+    out = b200attn.attention_forward(q.to(cuda), k.to(cuda), v.to(cuda), None, None, w.to(cuda),
+                                     w.to(cuda), torch.from_numpy(pe).to(cuda), desc=desc,
+                                     row_limit=torch.from_numpy(limits).to(cuda),
+                                     k_rot_out=k_rot, v_out=v_out)
+    torch.cuda.synchronize()
+    kv = np.ones((1, P), np.uint8)
+    kv[0, pv:] = 0
+    mask = ref.block_causal_mask(ids, kv if pad else None, 1)
+    qh = ref.apply_rope(np.transpose(ref.rms_norm(f32np(q), w.numpy()), (0, 2, 1, 3)), pe)
+    kh = ref.apply_rope(np.transpose(ref.rms_norm(f32np(k), w.numpy()), (0, 2, 1, 3)), pe)
+    vh = np.transpose(f32np(v), (0, 2, 1, 3))
+    want = np.transpose(ref.chunked_attention(qh, kh, vh, 128 ** -0.5, mask), (0, 2, 1, 3))
+    check(f32np(out), want.reshape(1, P, H * 128))
+    check(f32np(k_rot), kh, rel=3e-3)
+    assert np.array_equal(f32np(v_out), vh)
