@@ -41,6 +41,10 @@ CONFIGS = {
     # 2048^2: heads sharded 32/N per GPU, to_out partial sums all-reduced (one block per step)
     "c4": dict(grid=(128, 128), P=512, pv=None, layers=1, cond=[], hidden=4096,
                name="2048^2 T2I, head-sharded (config 4)"),
+    # the full 32-block denoising loop: 8 prompts (text lengths ~ U[64, 512]) x true CFG
+    # = 16 sequences at 1024^2, data-parallel over ranks by prompt (pos/neg stay together)
+    "c5": dict(grid=(64, 64), prompts=8, len_range=(64, 512), layers=32, cfg_scale=4.0,
+               denoise_steps=20, name="1024^2 denoising loop, 8 prompts x CFG (config 5)"),
 }
 
 
@@ -238,7 +242,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference(args, rank)
+        if args.config == "c5":
+            run_reference_denoise(args, rank)
+        else:
+            run_reference(args, rank)
         return
 
     import numpy as np
@@ -256,6 +263,9 @@ def main():
     cfg = CONFIGS[args.config]
     if args.config == "c4":
         run_head_sharded(args, cfg, rank, world, dev)
+        return
+    if args.config == "c5":
+        run_denoise(args, cfg, rank, world, dev)
         return
     gh, gw = cfg["grid"]
     T, P, L = gh * gw, cfg["P"], args.layers or cfg["layers"]
@@ -486,6 +496,221 @@ def run_head_sharded(args, cfg, rank, world, dev):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------- config 5
+C5_METRIC = "denoise-step ms at 1024^2 (config 5: 16 sequences = 8 prompts x CFG, 32 blocks)"
+
+
+def c5_workload(cfg):
+    """Seeded prompt lengths (pos, neg) of the 8 prompts, uniform in [64, 512]."""
+    import numpy as np
+    rng = np.random.default_rng(5)
+    lo, hi = cfg["len_range"]
+    return [(int(a), int(b)) for a, b in rng.integers(lo, hi + 1, size=(cfg["prompts"], 2))]
+
+
+def c5_flops(model_cfg, lengths, T):
+    """GEMM + attention FLOPs of one cached step of the given sequences."""
+    lin = model_cfg.linear_flops_per_token() * T * len(lengths)
+    lin += 2.0 * T * len(lengths) * model_cfg.hidden * model_cfg.in_channels * 2  # img_in, proj_out
+    attn = sum(4.0 * model_cfg.heads * T * (n + T) * HEAD_DIM for n in lengths) * model_cfg.layers
+    return lin, attn
+
+
+def run_denoise(args, cfg, rank, world, dev):
+    """Config 5: every rank runs the denoising loop of its prompts (both CFG branches),
+    batched through each block; a step is one Euler step of this rank's sequences.  Strong
+    scaling: the 8 prompts are split over the ranks; value = max over ranks of ms/step."""
+    import torch
+    import torch.distributed as dist
+
+    from b200attn import dist as bdist
+    from b200attn import mmdit
+
+    gh, gw = cfg["grid"]
+    T = gh * gw
+    mcfg = mmdit.MMDiTConfig(layers=args.layers or cfg["layers"])
+    pairs = c5_workload(cfg)
+    mine = bdist.dp_assign(list(range(cfg["prompts"])), world, rank)
+    lengths = [n for p in mine for n in pairs[p]]          # p0 pos, p0 neg, p1 pos, ...
+    weights = mmdit.random_weights(mcfg, 2024, device=dev, std=0.02)   # same on every rank
+    model = mmdit.MMDiT(mcfg, weights, device=dev)
+    del weights
+    g = torch.Generator(device=dev).manual_seed(77)
+    embs = [torch.randn(n, mcfg.text_dim, generator=g, device=dev).to(torch.bfloat16)
+            for p in range(cfg["prompts"]) for n in pairs[p]]
+    embs = [embs[2 * p + j] for p in mine for j in range(2)]
+    noise = torch.randn(cfg["prompts"], T, mcfg.in_channels, generator=g, device=dev)[mine]
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # prefix fill (once per prompt, outside the step) and the step's fixed inputs
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    cache = model.prefix_fill(embs)
+    f1.record(stream)
+    pe = model.target_pe(cache.lengths, (gh, gw))
+    desc = mmdit.cached_desc(cache, T, dev)
+    sig = mmdit.flow_match_sigmas(cfg["denoise_steps"], T)
+    lat = noise.clone()
+
+    def step(i):
+        nonlocal lat
+        k = i % cfg["denoise_steps"]
+        pred = model.step(lat.repeat_interleave(2, 0), float(sig[k]), cache, pe, desc)
+        pos, neg = pred[0::2], pred[1::2]
+        lat = lat + (neg + (pos - neg) * cfg["cfg_scale"]) * mmdit.euler_dt(sig, k)
+
+    for i in range(args.warmup):
+        step(i)
+    barrier()
+    prefix_ms = f0.elapsed_time(f1)
+    model.attn_marks = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    with ClockSampler(uuid) as clocks:
+        barrier()
+        e0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        e1.record(stream)
+        barrier()
+    marks, model.attn_marks = model.attn_marks, None
+    ms_rank = e0.elapsed_time(e1) / args.steps
+    attn_ms_rank = sum(a.elapsed_time(b) for a, b in marks) / args.steps
+    if not torch.isfinite(lat).all():
+        raise RuntimeError("non-finite latents in the denoising loop")
+
+    # ---- end to end: the public denoise() call from host prompt embeddings and noise to
+    # host latents, prefix fill included, over the full 20-step schedule
+    e2e = None
+    if args.e2e_steps > 0:
+        host_embs = [e.cpu().pin_memory() for e in embs]
+        host_noise = noise.cpu().pin_memory()
+        n_steps = cfg["denoise_steps"]
+        barrier()
+        e0.record(stream)
+        out = mmdit.denoise(model, host_embs[0::2], host_embs[1::2], (gh, gw), n_steps,
+                            cfg["cfg_scale"], host_noise)
+        host_lat = out.cpu()
+        e1.record(stream)
+        barrier()
+        e2e_rank = e0.elapsed_time(e1) / n_steps
+        h2d = sum(e.numel() * 2 for e in host_embs) + host_noise.numel() * 4
+        e2e = dict(ms=e2e_rank, h2d=h2d, d2h=host_lat.numel() * 4, steps=n_steps)
+
+    vals = torch.tensor([ms_rank, attn_ms_rank, prefix_ms, e2e["ms"] if e2e else 0.0],
+                        dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms_step, attn_ms, prefix_ms_max, e2e_ms = (float(v) for v in vals)
+    all_lengths = [n for p in range(cfg["prompts"]) for n in pairs[p]]
+    lin_f, attn_f = c5_flops(mcfg, all_lengths, T)
+    my_lin, my_attn = c5_flops(mcfg, lengths, T)
+    if rank == 0:
+        pk_d, src = peaks()
+        peak = float(pk_d.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+        attn_achieved = my_attn / (attn_ms_rank / 1e3) / 1e12
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline_denoise(cfg, all_lengths)
+        line = {
+            "metric": C5_METRIC, "value": ms_step, "unit": "ms", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init N(0,0.02) bf16 weights, seeded N(0,1) prompt "
+                    "embeddings and noise)",
+            "config": {"workload": cfg["name"], "T": T, "prompts": cfg["prompts"],
+                       "sequences": 2 * cfg["prompts"], "prompt_lengths": pairs,
+                       "blocks": mcfg.layers, "hidden": mcfg.hidden, "ffn": mcfg.ffn,
+                       "weights": "bf16 (7.1 B parameters)", "cfg_scale": cfg["cfg_scale"],
+                       "parallelism": f"dp{world} by prompt (pos/neg pairs together)",
+                       "l2": "every step streams 14 GB of weights and GBs of activations (> L2)"},
+            "step_tflops": (lin_f + attn_f) / (ms_step / 1e3) / 1e12,
+            "pct_bf16_peak": 100.0 * (lin_f + attn_f) / world / (ms_step / 1e3) / 1e12 / peak,
+            "attention_ms_per_step": attn_ms, "attention_share": attn_ms / ms_step,
+            "prefix_fill_ms": prefix_ms_max,
+            "roofline": {"bound": "tensor", "achieved": attn_achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": attn_achieved / peak, "traffic": None,
+                         "kernel": "b200_attn_fwd span (norm_rope + joint_attn_kernel) in the loop",
+                         "peak_source": f"{src} bf16_tflops_sustained"},
+            "cpu_baseline": cpu,
+            "e2e": None if e2e is None else {
+                "value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": e2e["h2d"] // e2e["steps"],
+                "d2h_bytes_per_step": e2e["d2h"] // e2e["steps"],
+                "path": "mmdit.denoise(): host embeddings + noise in, prefix fill, 20 steps, "
+                        "host latents out; ms per step"},
+            "clocks": clocks.summary(),
+            # per block: 2 residual/norm kernels, 2 attention launches, 1 swiglu per MLP
+            # chunk; plus block 0's norm1 (GEMMs are cuBLAS, not counted)
+            "gpu_launches": args.steps * (mcfg.layers * (4 + -(-T * len(lengths) // model.mlp_chunk_rows)) + 1),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _denoise_cpu_sample(cfg, length):
+    """Seconds of one cached block of one sequence at full width on the host's cores, with
+    the float32 oracle (a 1-block model; weights N(0, 0.02))."""
+    import torch
+    from b200attn import mmdit
+    from oracle import mmdit_ref as M  # CPU baseline leg (test / baseline infrastructure)
+    torch.set_num_threads(os.cpu_count() or 1)
+    gh, gw = cfg["grid"]
+    one = mmdit.MMDiTConfig(layers=1)
+    R = M.Reference(mmdit.random_weights(one, 1), one.layers, one.heads)
+    g = torch.Generator().manual_seed(3)
+    emb = torch.randn(length, one.text_dim, generator=g)
+    lat = torch.randn(gh * gw, one.in_channels, generator=g)
+    cache = R.prefix_kv(emb, (gh, gw))
+    R.forward_cached(lat[:256], 0.5, cache, length, (16, 16))  # warm the thread pool
+    t0 = time.perf_counter()
+    R.forward_cached(lat, 0.5, cache, length, (gh, gw))
+    return time.perf_counter() - t0
+
+
+def cpu_baseline_denoise(cfg, lengths):
+    """The float32 oracle on the host: one block of one mean-length sequence, scaled to a
+    step of 16 sequences x 32 blocks."""
+    n = int(round(sum(lengths) / len(lengths)))
+    dt = _denoise_cpu_sample(cfg, n)
+    ms = dt * 1e3 * len(lengths) * CONFIGS["c5"]["layers"]
+    return {"value": ms, "unit": "ms", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"1 of 32 blocks of 1 of {len(lengths)} sequences (prompt {n} tokens, "
+                      f"{dt:.1f} s, float32 torch oracle), scaled x{len(lengths) * 32}"}
+
+
+def run_reference_denoise(args, rank):
+    """Config 5 on the host cores with the float32 oracle (bounded sample, see above)."""
+    if rank != 0:
+        return
+    cfg = CONFIGS["c5"]
+    lengths = [n for pair in c5_workload(cfg) for n in pair]
+    n = int(round(sum(lengths) / len(lengths)))
+    for _ in range(min(args.warmup, 1)):
+        _denoise_cpu_sample(cfg, n)
+    samples = [_denoise_cpu_sample(cfg, n) for _ in range(max(1, min(args.steps, 3)))]
+    ms = statistics.median(samples) * 1e3 * len(lengths) * cfg["layers"]
+    sample = (f"1 of 32 blocks of 1 of {len(lengths)} sequences per step (prompt {n} tokens, "
+              f"float32 torch oracle), scaled x{len(lengths) * 32}")
+    print(json.dumps({
+        "impl": "reference", "metric": C5_METRIC, "value": ms, "unit": "ms",
+        "n_gpus": args.gpus, "steps": len(samples), "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (random-init weights, seeded embeddings and noise)",
+        "config": {"workload": cfg["name"] + " sample", "T": cfg["grid"][0] * cfg["grid"][1]},
+        "cpu_baseline": {"value": ms, "unit": "ms", "cores": os.cpu_count() or 1, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": ms, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
 
 
 if __name__ == "__main__":

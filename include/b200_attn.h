@@ -30,7 +30,7 @@ extern "C" {
 #endif
 
 #define B200_ATTN_HEAD_DIM 128
-#define B200_ATTN_ABI_VERSION 2
+#define B200_ATTN_ABI_VERSION 3
 
 typedef enum {
   B200_OK = 0,
@@ -93,6 +93,11 @@ typedef struct {
                           passes b200_block_causal_limits() of its layout with
                           prefix_len = 0, which replaces build_block_causal_mask
                           (src/attention_mask.rs:18-66, src/transformer.rs:696-702)  */
+  int64_t pe_batch_stride; /* floats between the pe rows of consecutive batch rows: 0 =
+                          one [T,D] table for every row (the reference: one layout per
+                          call, src/transformer.rs:729-734); T*D = a [B,T,D] table, for a
+                          batch of prompts with different prefix lengths, whose target
+                          tokens differ in the RoPE frame position.  Multiple of 4.    */
 } b200_attn_args;
 
 /*

@@ -32,6 +32,7 @@ EXPORTED = (
     "b200_joint_layout", "b200_rope_positions", "b200_rope_pe", "b200_key_valid_to_desc",
     "b200_block_causal_limits",
     "b200_strerror", "b200_abi_version",
+    "b200_residual_adaln", "b200_swiglu",
 )
 
 
@@ -58,7 +59,7 @@ class AttnArgs(ctypes.Structure):
         ("scale", ctypes.c_float), ("out", ctypes.c_void_p), ("k_rot_out", ctypes.c_void_p),
         ("v_out", ctypes.c_void_p), ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t), ("status", ctypes.c_void_p),
-        ("row_limit", ctypes.c_void_p),
+        ("row_limit", ctypes.c_void_p), ("pe_batch_stride", ctypes.c_int64),
     ]
 
 
@@ -85,6 +86,9 @@ def lib() -> ctypes.CDLL:
         L.b200_rope_pe.argtypes = [vp, i32, vp, i32, vp, f32, vp]
         L.b200_key_valid_to_desc.argtypes = [vp, i32, i32, i32, vp]
         L.b200_block_causal_limits.argtypes = [vp, i32, vp]
+        i64 = ctypes.c_int64
+        L.b200_residual_adaln.argtypes = [vp, vp, vp, vp, vp, i64, i32, i64, i64, f32, vp]
+        L.b200_swiglu.argtypes = [vp, vp, i64, i32, vp]
         L.b200_strerror.argtypes = [ctypes.c_int]
         L.b200_strerror.restype = ctypes.c_char_p
         for name in EXPORTED:
@@ -192,6 +196,8 @@ def make_args(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w, pe, out, desc=Non
     a.norm_q_w, a.norm_k_w = _dptr(norm_q_w), _dptr(norm_k_w)
     a.norm_eps = eps
     a.pe = _dptr(pe)
+    # pe [T, D] is shared by the batch rows; pe [B, T, D] gives each row its own table.
+    a.pe_batch_stride = pe.shape[-2] * pe.shape[-1] if pe is not None and pe.dim() == 3 else 0
     a.desc = _dptr(desc)
     a.scale = d ** -0.5 if scale is None else scale
     a.out = _dptr(out)
@@ -215,7 +221,8 @@ def attention_forward(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w, pe, desc=
     """The Attention::forward span from the norm to the head merge on the GPU.
 
     q, k, v: bf16 [B,T,H,D] raw projections; prefix_k/v: bf16 [B,H,P,D] (or None);
-    norm weights f32 [D]; pe f32 [T,D]; desc int32 [B,2] device tensor or None.
+    norm weights f32 [D]; pe f32 [T,D] (or [B,T,D], one table per batch row); desc int32
+    [B,2] device tensor or None.
     Returns out bf16 [B,T,H*D].
     """
     import torch
@@ -310,3 +317,33 @@ def joint_attention(q_rot, k_rot, v, prefix_k, prefix_v, desc=None, scale=None, 
                                       _dptr(workspace), ws_bytes, _dptr(status), _stream(stream)),
            "b200_joint_attention")
     return out
+
+
+# ----------------------------------------------------------------- block elementwise steps
+def residual_adaln(x, y, gate, scale, out, rows_per_mod: int, eps: float = 1e-6, stream=None):
+    """x += tanh(gate) * y (if y is given); out = LayerNorm(x) * (1 + scale) (if out is given).
+
+    x f32 [R, C] (updated in place); y bf16 [R, C] or None; gate / scale f32 rows of one
+    modulation matrix [n_mod, ...] (row stride taken from the tensor) selected by
+    r // rows_per_mod; out bf16 [R, C] or None.  (src/transformer.rs:407-424, 448-454)
+    """
+    cols = x.shape[-1]
+    rows = x.numel() // cols
+    strides = {t.stride(0) if t.dim() > 1 else 0 for t in (gate, scale) if t is not None}
+    if len(strides) > 1 and rows > rows_per_mod:
+        raise ValueError("gate and scale must be rows of one modulation matrix")
+    stride = max(strides) if rows > rows_per_mod else 0
+    _check(lib().b200_residual_adaln(_dptr(x), _dptr(y), _dptr(gate), _dptr(scale), _dptr(out),
+                                     rows, cols, int(rows_per_mod), stride, float(eps),
+                                     _stream(stream)), "b200_residual_adaln")
+    return out
+
+
+def swiglu(gp, h=None, stream=None):
+    """h = silu(gp[:, :F]) * gp[:, F:] for gp bf16 [R, 2F] (src/transformer.rs:326-331)."""
+    import torch
+    rows, f2 = gp.numel() // gp.shape[-1], gp.shape[-1]
+    if h is None:
+        h = torch.empty((rows, f2 // 2), dtype=torch.bfloat16, device=gp.device)
+    _check(lib().b200_swiglu(_dptr(gp), _dptr(h), rows, f2 // 2, _stream(stream)), "b200_swiglu")
+    return h

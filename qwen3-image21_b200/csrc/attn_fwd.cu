@@ -652,8 +652,8 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
 __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeJob j0, NormRopeJob j1,
                                                          NormRopeJob j2, int B, int T, int H,
                                                          float eps, const float* pe,
-                                                         int rope_mask, int32_t* zero,
-                                                         int n_zero) {
+                                                         int64_t pe_bs, int rope_mask,
+                                                         int32_t* zero, int n_zero) {
   // Also clears the attention kernel's split arrival counters (n_zero <= 256), which saves
   // a separate memset before the attention launch that follows on the same stream.
   if (zero && blockIdx.x == 0 && blockIdx.y == 0 && static_cast<int>(threadIdx.x) < n_zero)
@@ -700,7 +700,7 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeJob j0, NormRope
     }
     if (row < rows) {
       if (rope) {
-        const float* pr = pe + static_cast<size_t>(t) * kD + sub * 8;
+        const float* pr = pe + static_cast<int64_t>(b) * pe_bs + static_cast<size_t>(t) * kD + sub * 8;
         const float4 ca = *reinterpret_cast<const float4*>(pr);
         const float4 cb = *reinterpret_cast<const float4*>(pr + 4);
         const float cs[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
@@ -864,7 +864,7 @@ int launch_attention(const CUtensorMap& mq, const CUtensorMap& mk0, const CUtens
 }
 
 int launch_norm_rope(const NormRopeJob* jobs, int njobs, int B, int T, int H, float eps,
-                     const float* pe, int rope_mask, cudaStream_t stream,
+                     const float* pe, int64_t pe_bs, int rope_mask, cudaStream_t stream,
                      int32_t* zero = nullptr, int n_zero = 0) {
   const int64_t rows = static_cast<int64_t>(B) * T * H;
   if (rows == 0 || njobs == 0) return B200_OK;
@@ -874,8 +874,8 @@ int launch_norm_rope(const NormRopeJob* jobs, int njobs, int B, int T, int H, fl
   if (blocks > 0x7fffffff) return B200_ERR_INVALID;
   NormRopeJob j[3] = {jobs[0], njobs > 1 ? jobs[1] : jobs[0], njobs > 2 ? jobs[2] : jobs[0]};
   dim3 grid(static_cast<unsigned>(blocks), njobs);
-  norm_rope_kernel<<<grid, 256, 0, stream>>>(j[0], j[1], j[2], B, T, H, eps, pe, rope_mask, zero,
-                                             n_zero);
+  norm_rope_kernel<<<grid, 256, 0, stream>>>(j[0], j[1], j[2], B, T, H, eps, pe, pe_bs, rope_mask,
+                                             zero, n_zero);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
@@ -942,6 +942,8 @@ extern "C" int b200_attn_fwd(const b200_attn_args* a, b200_stream_t stream_) {
     return B200_ERR_INVALID;
   if (a->prefix_len > 0 && (!a->prefix_k || !a->prefix_v)) return B200_ERR_INVALID;
   if (!(a->scale > 0.f) || !std::isfinite(a->scale)) return B200_ERR_INVALID;
+  // Per-batch RoPE rows must keep the 16-byte alignment of the float4 loads.
+  if (a->pe_batch_stride < 0 || a->pe_batch_stride % 4 != 0) return B200_ERR_INVALID;
   const void* ptrs[] = {a->q, a->k, a->v, a->out, a->norm_q_w, a->norm_k_w, a->pe,
                         a->workspace, a->k_rot_out, a->v_out, a->prefix_k, a->prefix_v};
   for (const void* ptr : ptrs)
@@ -967,8 +969,9 @@ extern "C" int b200_attn_fwd(const b200_attn_args* a, b200_stream_t stream_) {
                           ? reinterpret_cast<int32_t*>(static_cast<uint8_t*>(split_region) +
                                                        size_t{kMaxSplitSlots} * kSplitSlotBytes)
                           : nullptr;
-  int rc = launch_norm_rope(jobs, a->v_out ? 3 : 2, B, T, H, a->norm_eps, a->pe, 0x3, stream,
-                            counters, counters ? kMaxSplitSlots : 0);
+  int rc = launch_norm_rope(jobs, a->v_out ? 3 : 2, B, T, H, a->norm_eps, a->pe,
+                            a->pe_batch_stride, 0x3, stream, counters,
+                            counters ? kMaxSplitSlots : 0);
   if (rc != B200_OK) return rc;
 
   return joint_attention(q_rot, k_rot, a->v, a->prefix_k, a->prefix_v, B, H, T, P, a->desc,
@@ -1037,7 +1040,7 @@ extern "C" int b200_norm_rope(const void* x, void* y, int32_t batch, int32_t tok
   if (!x || !y || !aligned16(x) || !aligned16(y)) return B200_ERR_INVALID;
   if ((norm_w && !aligned16(norm_w)) || (pe && !aligned16(pe))) return B200_ERR_INVALID;
   NormRopeJob job{static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), norm_w};
-  return launch_norm_rope(&job, 1, batch, tokens, heads, eps, pe, 0x1,
+  return launch_norm_rope(&job, 1, batch, tokens, heads, eps, pe, 0, 0x1,
                           static_cast<cudaStream_t>(stream));
 }
 
@@ -1053,7 +1056,7 @@ extern "C" int b200_qk_norm_rope(const void* q, const void* k, void* q_rot, void
   NormRopeJob jobs[2] = {
       {static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(q_rot), norm_q_w},
       {static_cast<const __nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(k_rot), norm_k_w}};
-  return launch_norm_rope(jobs, 2, batch, tokens, heads, eps, pe, 0x3,
+  return launch_norm_rope(jobs, 2, batch, tokens, heads, eps, pe, 0, 0x3,
                           static_cast<cudaStream_t>(stream));
 }
 
