@@ -163,7 +163,8 @@ def random_weights(cfg: MMDiTConfig, seed: int, device="cpu", std: float = 0.02)
 class PrefixCache:
     """Per-layer post-RoPE K and V of every sequence's prefix, [B, H, Pmax, D] bf16 (the
     TextKvCache of src/transformer.rs:14-19, one tensor per layer for the whole batch;
-    rows past a sequence's own length are zero and masked by its descriptor)."""
+    rows past a sequence's own length hold its padding tokens' finite K/V, which every
+    cached step masks through the sequence's descriptor)."""
     k: List
     v: List
     lengths: List[int]

@@ -175,7 +175,9 @@ def test_prefix_fill_matches_oracle(tiny):
             v = cache.v[i][b, :, :n].float().cpu()
             assert rel(k, want[i][0]) < 1.5e-2, (b, i)   # bf16 GEMM operands: ~7e-3
             assert rel(v, want[i][1]) < 1.5e-2, (b, i)
-            assert cache.k[i][b, :, n:].abs().max().item() == 0 or n == max(lengths)
+            # rows past the prompt hold the padding tokens' K/V: finite, and masked by the
+            # sequence's descriptor in every later step
+            assert torch.isfinite(cache.k[i][b].float()).all() and torch.isfinite(cache.v[i][b].float()).all()
 
 
 @pytest.mark.gpu
