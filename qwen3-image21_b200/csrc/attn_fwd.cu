@@ -155,7 +155,8 @@ constexpr int kPolyEvery = 4;
 // only when the row max exceeds it by more than kRescaleThreshold (lazy rescaling, as in
 // FlashAttention-4), so P = 2^(S*c - m) <= 2^8.  P goes to TMEM columns [tS, tS + 64) as
 // bf16 pairs, over S columns already read.  Updates the running sum l and returns the
-// factor the O accumulator must be scaled by (1 when m did not move).
+// factor the O accumulator must be scaled by (1 when m did not move).  A row without any
+// valid key so far keeps m = -inf, P = 0 and l = 0.
 template <bool kMasked>
 __device__ __forceinline__ float softmax_row(const int valid, const float c, float& m, float& l,
                                              const uint32_t tS) {
@@ -186,7 +187,10 @@ __device__ __forceinline__ float softmax_row(const int valid, const float c, flo
     m = mx;
   }
   const uint64_t cc = f2pack(c, c);
-  const uint64_t nm = f2pack(-m, -m);
+  // A row that has not seen a valid key keeps m = -inf; its masked S (-inf) must give
+  // P = 2^-inf = 0, not 2^(-inf + inf) = NaN (a tail-split piece can hold such rows).
+  const float m_ref = m == -INFINITY ? 0.f : m;
+  const uint64_t nm = f2pack(-m_ref, -m_ref);
   uint64_t acc[4] = {f2pack(0.f, 0.f), f2pack(0.f, 0.f), f2pack(0.f, 0.f), f2pack(0.f, 0.f)};
 #pragma unroll
   for (int half = 0; half < 2; ++half) {

@@ -288,6 +288,35 @@ def test_tail_split_matches_oracle(cuda, T, P, pv, extra):
     _check_heads(out_split, h, [0, H - 3, H - 2, H - 1])  # the last items are the split ones
 
 
+def test_prefix_fill_tail_split_rows_without_keys(cuda):
+    """Causal prefix fill whose last partial wave is split by key tiles: a piece can hold
+    rows that see none of its keys (rows 0..127 of a first query block in the piece of keys
+    128..255).  Such rows contribute nothing to the merge; the output stays finite and
+    matches the oracle."""
+    torch = _torch()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    T, nqb = 512, 2
+    H = (sms + 4 + nqb - 1) // nqb          # items = 2H lands 4 past a full wave: split 2
+    lay = ref.joint_layout(T, None, [], (0, 0))
+    limits = b200attn.block_causal_limits(lay["image_ids"][:T])
+    pe = ref.embed_nd(lay["img_shapes"], lay["image_pad_mask"])[:T]
+    g = torch.Generator().manual_seed(77)
+    q, k, v = (bf16(torch.randn(1, T, H, 128, generator=g)) for _ in range(3))
+    w = torch.ones(128)
+    out = b200attn.attention_forward(q.to(cuda), k.to(cuda), v.to(cuda), None, None, w.to(cuda),
+                                     w.to(cuda), torch.from_numpy(pe).to(cuda),
+                                     row_limit=torch.from_numpy(limits).to(cuda))
+    torch.cuda.synchronize()
+    got = f32np(out).reshape(1, T, H, 128)
+    assert np.isfinite(got).all()
+    heads = [0, H - 2, H - 1]               # the last heads' items are the split ones
+    mask = ref.block_causal_mask(lay["image_ids"][:T], None, 1)
+    qh = ref.apply_rope(np.transpose(ref.rms_norm(f32np(q[:, :, heads]), w.numpy()), (0, 2, 1, 3)), pe)
+    kh = ref.apply_rope(np.transpose(ref.rms_norm(f32np(k[:, :, heads]), w.numpy()), (0, 2, 1, 3)), pe)
+    vh = np.transpose(f32np(v[:, :, heads]), (0, 2, 1, 3))
+    want = np.transpose(ref.chunked_attention(qh, kh, vh, 128 ** -0.5, mask), (0, 2, 1, 3))
+    check(got[:, :, heads].reshape(1, T, -1), want.reshape(1, T, -1))
+
 
 # ------------------------------------------------------------------ prefix fill (block-causal)
 @pytest.mark.parametrize("cond,pad", [([], 0), ([(8, 16), (16, 16)], 7), ([(16, 16)], 0)])
