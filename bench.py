@@ -79,6 +79,8 @@ def parse_args():
                     help="blocks per step (default 32; fewer only for profiling runs)")
     ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--weights", choices=["q4_k_m", "bf16"], default="q4_k_m",
+                    help="config 5: block linears as GGUF Q4_K_M blocks (the config) or bf16")
     return ap.parse_args()
 
 
@@ -535,8 +537,10 @@ def run_denoise(args, cfg, rank, world, dev):
     mine = bdist.dp_assign(list(range(cfg["prompts"])), world, rank)
     lengths = [n for p in mine for n in pairs[p]]          # p0 pos, p0 neg, p1 pos, ...
     weights = mmdit.random_weights(mcfg, 2024, device=dev, std=0.02)   # same on every rank
-    model = mmdit.MMDiT(mcfg, weights, device=dev)
+    model = mmdit.MMDiT(mcfg, weights, device=dev, weight_format=args.weights)
     del weights
+    torch.cuda.empty_cache()
+    wbytes = model.weight_bytes()
     g = torch.Generator(device=dev).manual_seed(77)
     embs = [torch.randn(n, mcfg.text_dim, generator=g, device=dev).to(torch.bfloat16)
             for p in range(cfg["prompts"]) for n in pairs[p]]
@@ -624,14 +628,17 @@ def run_denoise(args, cfg, rank, world, dev):
             "metric": C5_METRIC, "value": ms_step, "unit": "ms", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (random-init N(0,0.02) bf16 weights, seeded N(0,1) prompt "
-                    "embeddings and noise)",
+            "data": "synthetic (random-init N(0,0.02) weights"
+                    + (" quantised to GGUF Q4_K_M" if args.weights == "q4_k_m" else " in bf16")
+                    + ", seeded N(0,1) prompt embeddings and noise)",
             "config": {"workload": cfg["name"], "T": T, "prompts": cfg["prompts"],
                        "sequences": 2 * cfg["prompts"], "prompt_lengths": pairs,
                        "blocks": mcfg.layers, "hidden": mcfg.hidden, "ffn": mcfg.ffn,
-                       "weights": "bf16 (7.1 B parameters)", "cfg_scale": cfg["cfg_scale"],
+                       "weights": (f"{args.weights}: block linears {wbytes / 1e9:.2f} GB "
+                                   f"(7.1 B parameters)"),
+                       "cfg_scale": cfg["cfg_scale"],
                        "parallelism": f"dp{world} by prompt (pos/neg pairs together)",
-                       "l2": "every step streams 14 GB of weights and GBs of activations (> L2)"},
+                       "l2": "every step streams GBs of weights and activations (> L2)"},
             "step_tflops": (lin_f + attn_f) / (ms_step / 1e3) / 1e12,
             "pct_bf16_peak": 100.0 * (lin_f + attn_f) / world / (ms_step / 1e3) / 1e12 / peak,
             "attention_ms_per_step": attn_ms, "attention_share": attn_ms / ms_step,
@@ -648,8 +655,10 @@ def run_denoise(args, cfg, rank, world, dev):
                         "host latents out; ms per step"},
             "clocks": clocks.summary(),
             # per block: 2 residual/norm kernels, 2 attention launches, 1 swiglu per MLP
-            # chunk; plus block 0's norm1 (GEMMs are cuBLAS, not counted)
-            "gpu_launches": args.steps * (mcfg.layers * (4 + -(-T * len(lengths) // model.mlp_chunk_rows)) + 1),
+            # chunk, 6 dequantisations (q4_k_m); plus block 0's norm1 (GEMMs are cuBLAS,
+            # not counted)
+            "gpu_launches": args.steps * (mcfg.layers * (4 + (6 if args.weights == "q4_k_m" else 0)
+                                                         + -(-T * len(lengths) // model.mlp_chunk_rows)) + 1),
         }
         print(json.dumps(line), flush=True)
     if world > 1:

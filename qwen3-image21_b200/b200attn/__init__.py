@@ -33,6 +33,7 @@ EXPORTED = (
     "b200_block_causal_limits",
     "b200_strerror", "b200_abi_version",
     "b200_residual_adaln", "b200_swiglu",
+    "b200_dequant_q4_k", "b200_dequant_q6_k",
 )
 
 
@@ -89,6 +90,8 @@ def lib() -> ctypes.CDLL:
         i64 = ctypes.c_int64
         L.b200_residual_adaln.argtypes = [vp, vp, vp, vp, vp, i64, i32, i64, i64, f32, vp]
         L.b200_swiglu.argtypes = [vp, vp, i64, i32, vp]
+        L.b200_dequant_q4_k.argtypes = [vp, vp, i64, vp]
+        L.b200_dequant_q6_k.argtypes = [vp, vp, i64, vp]
         L.b200_strerror.argtypes = [ctypes.c_int]
         L.b200_strerror.restype = ctypes.c_char_p
         for name in EXPORTED:
@@ -347,3 +350,20 @@ def swiglu(gp, h=None, stream=None):
         h = torch.empty((rows, f2 // 2), dtype=torch.bfloat16, device=gp.device)
     _check(lib().b200_swiglu(_dptr(gp), _dptr(h), rows, f2 // 2, _stream(stream)), "b200_swiglu")
     return h
+
+
+# ----------------------------------------------------------------- GGUF k-quant weights
+Q4_K_BLOCK_BYTES, Q6_K_BLOCK_BYTES, QK_K = 144, 210, 256
+
+
+def dequant(blocks, qtype: str, out=None, stream=None):
+    """GGUF k-quant super-blocks (uint8 [..., n_blocks * block_bytes]) -> bf16 [n_blocks * 256]
+    (viewed as the caller's shape when `out` is given).  qtype: "q4_k" or "q6_k"."""
+    import torch
+    nbytes = {"q4_k": Q4_K_BLOCK_BYTES, "q6_k": Q6_K_BLOCK_BYTES}[qtype]
+    n_blocks = blocks.numel() // nbytes
+    if out is None:
+        out = torch.empty(n_blocks * QK_K, dtype=torch.bfloat16, device=blocks.device)
+    fn = lib().b200_dequant_q4_k if qtype == "q4_k" else lib().b200_dequant_q6_k
+    _check(fn(_dptr(blocks), _dptr(out), n_blocks, _stream(stream)), f"b200_dequant_{qtype}")
+    return out

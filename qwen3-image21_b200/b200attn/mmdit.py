@@ -173,10 +173,19 @@ class PrefixCache:
 class MMDiT:
     """The transformer on one GPU with bf16 weights (see module docstring)."""
 
-    def __init__(self, cfg: MMDiTConfig, weights: dict, device="cuda", mlp_chunk_rows: int = 16384):
+    def __init__(self, cfg: MMDiTConfig, weights: dict, device="cuda", mlp_chunk_rows: int = 16384,
+                 weight_format: str = "bf16"):
+        """weight_format "bf16" keeps the block linears in bf16; "q4_k_m" stores them as GGUF
+        Q4_K / Q6_K super-blocks (llama.cpp's Q4_K_M rule) and dequantises each block's six
+        matrices to a bf16 scratch right before its GEMMs.  The other weights (img_in,
+        txt_in, timestep, modulation, norm_out, proj_out: 1 % of the parameters) stay
+        bf16 / f32 either way."""
         import torch
+        if weight_format not in ("bf16", "q4_k_m"):
+            raise ValueError(f"unknown weight format {weight_format!r}")
         self.cfg, self.device = cfg, torch.device(device)
         self.mlp_chunk_rows = mlp_chunk_rows
+        self.weight_format = weight_format
         dev = self.device
         bf = lambda n: weights[n].to(device=dev, dtype=torch.bfloat16).contiguous()
         f32 = lambda n: weights[n].to(device=dev, dtype=torch.float32).contiguous()
@@ -201,6 +210,17 @@ class MMDiT:
                 wgp=torch.cat([bf(p + "img_mlp.gate_layer.weight"),
                                bf(p + "img_mlp.proj.weight")], 0).contiguous(),
                 wmo=bf(p + "img_mlp.out.weight")))
+        if weight_format == "q4_k_m":
+            from b200attn import gguf as bq
+            # reference names of the block linears (the fused gate_up is one GGUF tensor in
+            # ComfyUI-style files, src/quantized_transformer.rs:160-166, output [gate; up])
+            names = dict(wq="to_q", wk="to_k", wv="to_v", wo="to_out", wgp="gate_up", wmo="out")
+            for i, blk in enumerate(self.blocks):
+                for key, name in names.items():
+                    w = blk.pop(key)
+                    qtype = bq.q4_k_m_type(name, i, cfg.layers)
+                    blk["q_" + key] = bq.QuantLinear(bq.quantize(w.float(), qtype), qtype, tuple(w.shape))
+                    del w
         self._bufs = {}
         # When a list, every attention call of the block loop appends its (start, end) CUDA
         # events (the b200_attn_fwd span: Q/K norm + RoPE prologue and attention kernel).
@@ -241,6 +261,48 @@ class MMDiT:
         import torch.nn.functional as F
         return F.silu(t_emb) @ self.norm_out_w.t()
 
+    def block_weights(self, i: int) -> dict:
+        """Block i's bf16 weights: the stored tensors, or (q4_k_m) its six linears
+        dequantised into this model's scratch buffers (valid until the next call)."""
+        import torch
+        blk = self.blocks[i]
+        if self.weight_format == "bf16":
+            return blk
+        out = dict(nq=blk["nq"], nk=blk["nk"])
+        for key in ("wq", "wk", "wv", "wo", "wgp", "wmo"):
+            ql = blk["q_" + key]
+            out[key] = ql.dequant_into(self._buf("dq_" + key, ql.shape, torch.bfloat16))
+        return out
+
+    def weight_bytes(self) -> int:
+        """HBM bytes of the block linears (the 99 % of the parameters they hold)."""
+        total = 0
+        for blk in self.blocks:
+            for key in ("wq", "wk", "wv", "wo", "wgp", "wmo"):
+                total += blk[key].numel() * 2 if key in blk else blk["q_" + key].nbytes()
+        return total
+
+    def effective_weights(self, weights: dict) -> dict:
+        """`weights` with each block linear replaced by the values this model multiplies by
+        (the bf16 dequantisation for q4_k_m), as float32 CPU tensors: what a float32
+        reference of this model must use."""
+        import torch
+        out = {k: v.detach().float().cpu() for k, v in weights.items()}
+        if self.weight_format == "bf16":
+            return out
+        names = dict(wq="attn.to_q", wk="attn.to_k", wv="attn.to_v", wo="attn.to_out.0",
+                     wmo="img_mlp.out")
+        f = self.cfg.ffn
+        for i in range(self.cfg.layers):
+            w = self.block_weights(i)
+            p = f"transformer_blocks.{i}."
+            for key, name in names.items():
+                out[p + name + ".weight"] = w[key].float().cpu()
+            gp = w["wgp"].float().cpu()
+            out[p + "img_mlp.gate_layer.weight"] = gp[:f].clone()
+            out[p + "img_mlp.proj.weight"] = gp[f:].clone()
+        return out
+
     def _gemm(self, a, w, name):
         """a [R, K] bf16 @ w[N, K]^T -> bf16 [R, N] (cuBLAS)."""
         import torch
@@ -264,7 +326,8 @@ class MMDiT:
         ws_need = 2 * B * H * T * HEAD_DIM * 2 + b200attn.SPLIT_WORKSPACE_BYTES + 4096
         ws = self._buf("ws", (ws_need,), torch.uint8)
         b200attn.residual_adaln(x, None, None, scale1, y, rows_per_mod=R)      # norm1 of block 0
-        for i, blk in enumerate(self.blocks):
+        for i in range(len(self.blocks)):
+            blk = self.block_weights(i)
             q = self._gemm(y, blk["wq"], "q").view(B, T, H, HEAD_DIM)
             k = self._gemm(y, blk["wk"], "k").view(B, T, H, HEAD_DIM)
             v = self._gemm(y, blk["wv"], "v").view(B, T, H, HEAD_DIM)
