@@ -251,6 +251,15 @@ const char* b200_strerror(int status);
 /* ABI version (B200_ATTN_ABI_VERSION). */
 int b200_abi_version(void);
 
+/*
+ * Self-test of the device-side failure path (no counterpart in the reference): one small
+ * kernel waits on a barrier that nothing completes, with the same bounded wait and CTA
+ * abort flag as the attention kernel.  After the wait gives up (limit_us, at most 2 s),
+ * status[0] = 1 (the wait ran out) and status[1] = 1 (a second waiter left on the abort
+ * flag); status (device int32[2]) must be zero before the call.  The context stays usable.
+ */
+int b200_wait_selftest(int32_t* status, uint32_t limit_us, b200_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

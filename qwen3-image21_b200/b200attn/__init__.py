@@ -33,7 +33,7 @@ EXPORTED = (
     "b200_block_causal_limits",
     "b200_strerror", "b200_abi_version",
     "b200_residual_adaln", "b200_swiglu",
-    "b200_dequant_q4_k", "b200_dequant_q6_k",
+    "b200_dequant_q4_k", "b200_dequant_q6_k", "b200_wait_selftest",
 )
 
 
@@ -92,6 +92,7 @@ def lib() -> ctypes.CDLL:
         L.b200_swiglu.argtypes = [vp, vp, i64, i32, vp]
         L.b200_dequant_q4_k.argtypes = [vp, vp, i64, vp]
         L.b200_dequant_q6_k.argtypes = [vp, vp, i64, vp]
+        L.b200_wait_selftest.argtypes = [vp, ctypes.c_uint32, vp]
         L.b200_strerror.argtypes = [ctypes.c_int]
         L.b200_strerror.restype = ctypes.c_char_p
         for name in EXPORTED:
@@ -367,3 +368,13 @@ def dequant(blocks, qtype: str, out=None, stream=None):
     fn = lib().b200_dequant_q4_k if qtype == "q4_k" else lib().b200_dequant_q6_k
     _check(fn(_dptr(blocks), _dptr(out), n_blocks, _stream(stream)), f"b200_dequant_{qtype}")
     return out
+
+
+def wait_selftest(limit_us: int = 20000, stream=None):
+    """Runs the device-side bounded-wait self-test; returns the two status words
+    (1, 1 when a wait ran out and the abort flag released the other waiter)."""
+    import torch
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
+    _check(lib().b200_wait_selftest(_dptr(status), int(limit_us), _stream(stream)),
+           "b200_wait_selftest")
+    return [int(x) for x in status.cpu()]

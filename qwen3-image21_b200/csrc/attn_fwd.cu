@@ -631,6 +631,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ wait self-test
+// The attention kernel's failure path on a wait that can never complete: warp 0 waits on
+// an mbarrier nothing arrives on, gives up after limit_ns, raises the CTA abort flag and
+// records status[0] = 1; warp 1, waiting on another such barrier with the abort flag (and
+// twice the limit as its own bound), must leave because of the flag and records
+// status[1] = 1 when it did.  Both waits end by construction.
+__global__ void __launch_bounds__(64) wait_selftest_kernel(int32_t* status, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ int abort_word;
+  volatile int* abort_flag = &abort_word;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    if (!mbar_wait(&bars[0], 0, nullptr, limit_ns)) {
+      *abort_flag = 1;
+      atomicCAS(status, 0, 1);
+    }
+  } else if (threadIdx.x == 32 && lane == 0) {
+    const uint64_t t0 = global_timer_ns();
+    const bool done = mbar_wait(&bars[1], 0, abort_flag, 2 * limit_ns);
+    if (!done && *abort_flag && global_timer_ns() - t0 < 2 * limit_ns) atomicCAS(status + 1, 0, 1);
+  }
+  __syncthreads();
+}
+
 // ------------------------------------------------------------------ norm + RoPE
 // A group of 16 lanes handles kNormRows consecutive (b, t, h) rows of 128 values; lane i
 // of the group owns elements 8i..8i+7 (RoPE pairs 4i..4i+3) and all loads of the group's
@@ -1109,4 +1140,12 @@ extern "C" int b200_attn_fwd_noalloc(const b200_attn_args* args, b200_stream_t s
   a.workspace = scratch;
   a.workspace_bytes = B200_NOALLOC_SCRATCH_BYTES;
   return b200_attn_fwd(&a, stream);
+}
+
+extern "C" int b200_wait_selftest(int32_t* status, uint32_t limit_us, b200_stream_t stream) {
+  if (!status || limit_us == 0 || limit_us > 2000000u) return B200_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(status) & 3u) return B200_ERR_INVALID;
+  wait_selftest_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(
+      status, static_cast<uint64_t>(limit_us) * 1000ull);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }

@@ -55,14 +55,15 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // out (kWaitLimitNs) or, when `abort_flag` is given, as soon as it is set — the caller
 // records an error and unwinds.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag = nullptr) {
+                                          volatile int* abort_flag = nullptr,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (abort_flag && *abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+      if (global_timer_ns() - t0 > limit_ns) return false;
     }
   }
 }
