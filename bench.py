@@ -413,8 +413,12 @@ def main():
 
 
 def run_head_sharded(args, cfg, rank, world, dev):
-    """Config 4: each rank runs the attention of its 32/N heads, its share of to_out, and
-    one NCCL all-reduce of the partial sums; a step is one block (strong scaling)."""
+    """Config 4: each rank runs the attention of its 32/N heads and its share of to_out; a
+    step is one block (strong scaling).  Two ways to sum the to_out partials are timed
+    back to back: the fused one (value) — the tcgen05 out-projection GEMM whose epilogue
+    stores every partial tile into the rank owning its rows, then the owners' sum and
+    broadcast (ScatterOutProj) — and the baseline, a cuBLAS GEMM followed by an NCCL
+    all-reduce.  On one GPU both are a plain GEMM."""
     import torch
     import torch.distributed as dist
 
@@ -431,6 +435,7 @@ def run_head_sharded(args, cfg, rank, world, dev):
     pk, pv = randn(1, hl, P, HEAD_DIM), randn(1, hl, P, HEAD_DIM)
     gw_ = torch.Generator(device=dev).manual_seed(99)  # to_out weights identical on every rank
     w_out = (0.02 * torch.randn(hidden, HEADS * HEAD_DIM, generator=gw_, device=dev)).to(torch.bfloat16)
+    w_cols = w_out[:, h0 * HEAD_DIM:h1 * HEAD_DIM]
     lay = b200attn.joint_layout(P, None, [], (gh, gw))
     pe = torch.from_numpy(b200attn.rope_pe(lay["img_shapes"], lay["image_pad_mask"])[P:]).to(dev)
     ones = torch.ones(HEAD_DIM, device=dev, dtype=torch.float32)
@@ -438,40 +443,75 @@ def run_head_sharded(args, cfg, rank, world, dev):
     k_rot = torch.empty_like(q_rot)
     attn = torch.empty(1, T, hl * HEAD_DIM, dtype=torch.bfloat16, device=dev)
     split_ws = torch.empty(b200attn.SPLIT_WORKSPACE_BYTES, dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
+    fused = None
+    fused_note = "plain tcgen05 GEMM (one GPU)"
+    if world > 1:
+        try:
+            fused = bdist.ScatterOutProj(T, hidden, dev)
+            fused_note = ("tcgen05 GEMM whose epilogue reduce-scatters over NVLink + "
+                          "owner sum / broadcast kernel")
+        except RuntimeError as e:
+            fused_note = f"no symmetric memory ({e}); fused path = NCCL path"
+    out_bf16 = torch.empty(T, hidden, dtype=torch.bfloat16, device=dev)
 
-    def step(mark=None):
+    def attention(mark=None):
         b200attn.qk_norm_rope(q, k, ones, ones, 1e-6, pe, q_rot, k_rot, stream=stream)
         if mark is not None:
             mark[0].record(stream)
         b200attn.joint_attention(q_rot, k_rot, v, pk, pv, out=attn, workspace=split_ws,
-                                 stream=stream)
+                                 status=status, stream=stream)
         if mark is not None:
             mark[1].record(stream)
-        part = bdist.out_proj_partial(attn.view(T, hl * HEAD_DIM), w_out, h0, h1, HEAD_DIM)
+        return attn.view(T, hl * HEAD_DIM)
+
+    def step_fused(mark=None):
+        a = attention(mark)
+        if fused is not None:
+            return fused(a, w_out, h0, h1, status=status)
+        if world == 1:
+            return b200attn.gemm(a, w_cols, out=out_bf16, status=status)
+        return step_nccl_tail(a)
+
+    def step_nccl_tail(a):
+        part = bdist.out_proj_partial(a, w_out, h0, h1, HEAD_DIM)
         bdist.allreduce_sum_(part)
         return part
+
+    def step_nccl(mark=None):
+        return step_nccl_tail(attention(mark))
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    for _ in range(args.warmup):
-        step()
-    barrier()
-    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
-    with ClockSampler(uuid) as clocks:
+    def timed(fn, steps, marks=None):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         e0.record(stream)
-        for s_ in range(args.steps):
-            step(marks[s_])
+        for s_ in range(steps):
+            fn(marks[s_] if marks is not None else None)
         e1.record(stream)
         barrier()
-    ms_step = bdist.max_over_ranks(e0.elapsed_time(e1) / args.steps, device=dev)
-    attn_ms = bdist.max_over_ranks(sum(m[0].elapsed_time(m[1]) for m in marks) / args.steps, device=dev)
+        return e0.elapsed_time(e1) / steps
+
+    for _ in range(args.warmup):
+        step_fused()
+        step_nccl()
+    barrier()
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    with ClockSampler(uuid) as clocks:
+        ms_fused = timed(step_fused, args.steps, marks)
+    attn_ms = sum(m[0].elapsed_time(m[1]) for m in marks) / args.steps
+    ms_nccl = timed(step_nccl, args.steps)
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device wait ran out during the bench (status {int(status.item())})")
+    ms_step = bdist.max_over_ranks(ms_fused, device=dev)
+    ms_nccl = bdist.max_over_ranks(ms_nccl, device=dev)
+    attn_ms = bdist.max_over_ranks(attn_ms, device=dev)
     attn_flops = 4.0 * HEADS * T * (P + T) * HEAD_DIM
     proj_flops = 2.0 * T * HEADS * HEAD_DIM * hidden
     if rank == 0:
@@ -486,15 +526,19 @@ def run_head_sharded(args, cfg, rank, world, dev):
             "data": "synthetic (seeded N(0,1) q/k/v and prefix cache, N(0,0.02) to_out)",
             "config": {"workload": cfg["name"] + ", one block per step", "T": T, "P": P,
                        "heads_per_gpu": hl, "head_dim": HEAD_DIM, "hidden": hidden,
-                       "parallelism": f"heads/{world} + NCCL all-reduce of to_out partials",
+                       "parallelism": f"heads/{world}; to_out partials summed by {fused_note}",
                        "l2": "inputs exceed L2"},
+            "nccl_path": {"ms_per_step": ms_nccl,
+                          "value": (attn_flops + proj_flops) / (ms_nccl / 1e3) / 1e12,
+                          "how": "cuBLAS to_out partial + NCCL all-reduce (bf16)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": None, "kernel": "joint_attn_kernel",
                          "peak_source": f"{src} bf16_tflops_sustained", "launch_ms": attn_ms},
             "cpu_baseline": None, "e2e": None, "clocks": clocks.summary(),
-            "gpu_launches": args.steps * 2,
+            "gpu_launches": args.steps * (4 if world > 1 else 3),
         }
         print(json.dumps(line), flush=True)
+    del fused
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

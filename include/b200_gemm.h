@@ -1,0 +1,73 @@
+/*
+ * b200_gemm.h — C = A · Bᵀ on the sm_100a tensor cores, and the out-projection of
+ * head-sharded attention fused with the reduction of its partial sums across GPUs.
+ *
+ * In the reference, `to_out` (src/transformer.rs:196) is one Linear on one GPU.  Sharding
+ * the heads over N GPUs gives each GPU the input columns of its heads, so each computes a
+ * full-width partial [T, hidden] and the N partials must be summed on every GPU (an
+ * all-reduce).  Here that is two launches per GPU around the caller's barriers:
+ *   1. b200_gemm_scatter: the GEMM's epilogue stores each partial tile, in bf16, straight
+ *      into the GPU that owns its rows (rows are split into N equal blocks), into that
+ *      owner's slot for this GPU — plain stores over NVLink, as soon as the tile is done
+ *      (the reduce-scatter traffic overlaps the GEMM);
+ *   2. b200_reduce_gather_bf16: each owner sums its N slots in f32 in a fixed order
+ *      (deterministic) and writes the bf16 rows into every GPU's output buffer.
+ * Per GPU each launch moves (N-1)/N of the output over NVLink, as a ring all-reduce does.
+ * The caller orders: every GPU done reading the previous output before (1); every GPU's
+ * (1) before any (2); every (2) before the output is read — e.g. a symmetric-memory or
+ * NCCL barrier between the launches.
+ *
+ * Conventions are those of b200_attn.h.
+ *   A: [M, K] bf16, row stride lda elements (lda >= K, lda % 8 == 0), 16-byte aligned
+ *   B: [N, K] bf16, row stride ldb (a Linear weight [out, in], or a column slice of one)
+ *   C: [M, N] with row stride ldc (ldc >= N, ldc % 8 == 0), 16-byte aligned
+ *   K % 8 == 0, N % 32 == 0; any M.
+ * status: optional device int32, set non-zero if a device-side wait ran out.
+ */
+#ifndef B200_GEMM_H
+#define B200_GEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "b200_attn.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_GEMM_STORE_BF16 0    /* C bf16 = A·Bᵀ                                       */
+#define B200_GEMM_RED_F32 1       /* C f32 += A·Bᵀ (red.global.add; C may be a peer's)    */
+#define B200_GEMM_SCATTER_BF16 2  /* internal: the epilogue of b200_gemm_scatter          */
+#define B200_GEMM_MAX_OWNERS 8
+
+int b200_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
+              int32_t m, int32_t n, int32_t k, int32_t mode, int32_t* status,
+              b200_stream_t stream);
+
+/*
+ * A · Bᵀ with row m stored (bf16) into owner q = m / rows_per_owner, slot src_slot:
+ * owner_bufs[q] + (src_slot * rows_per_owner + m - q * rows_per_owner) * ldc.
+ * owner_bufs: host array of n_owners (<= 8) device pointers (peer pointers for other
+ * GPUs), each a buffer of n_owners * rows_per_owner rows; n_owners * rows_per_owner >= M.
+ */
+int b200_gemm_scatter(const void* a, int64_t lda, const void* b, int64_t ldb,
+                      void* const* owner_bufs, int32_t n_owners, int32_t src_slot,
+                      int32_t rows_per_owner, int64_t ldc, int32_t m, int32_t n, int32_t k,
+                      int32_t* status, b200_stream_t stream);
+
+/*
+ * out[dst_row0 + r, :] = bf16(sum over s < n_src of slots[s * slot_rows + r, :]) for
+ * r < rows (<= slot_rows), written into each of the n_dst (<= 8) buffers dst_bufs (host
+ * array of device pointers, peer pointers for other GPUs).  slots: bf16
+ * [n_src * slot_rows, ld]; cols % 8 == 0.
+ */
+int b200_reduce_gather_bf16(const void* slots, int32_t n_src, int32_t slot_rows, int32_t rows,
+                            int32_t cols, int64_t ld, void* const* dst_bufs, int32_t n_dst,
+                            int64_t dst_row0, int64_t dst_ld, b200_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_GEMM_H */

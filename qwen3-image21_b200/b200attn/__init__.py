@@ -33,7 +33,8 @@ EXPORTED = (
     "b200_block_causal_limits",
     "b200_strerror", "b200_abi_version",
     "b200_residual_adaln", "b200_swiglu",
-    "b200_dequant_q4_k", "b200_dequant_q6_k", "b200_wait_selftest",
+    "b200_dequant_q4_k", "b200_dequant_q6_k", "b200_wait_selftest", "b200_gemm",
+    "b200_gemm_scatter", "b200_reduce_gather_bf16",
 )
 
 
@@ -93,6 +94,9 @@ def lib() -> ctypes.CDLL:
         L.b200_dequant_q4_k.argtypes = [vp, vp, i64, vp]
         L.b200_dequant_q6_k.argtypes = [vp, vp, i64, vp]
         L.b200_wait_selftest.argtypes = [vp, ctypes.c_uint32, vp]
+        L.b200_gemm.argtypes = [vp, i64, vp, i64, vp, i64, i32, i32, i32, i32, vp, vp]
+        L.b200_gemm_scatter.argtypes = [vp, i64, vp, i64, vp, i32, i32, i32, i64, i32, i32, i32, vp, vp]
+        L.b200_reduce_gather_bf16.argtypes = [vp, i32, i32, i32, i32, i64, vp, i32, i64, i64, vp]
         L.b200_strerror.argtypes = [ctypes.c_int]
         L.b200_strerror.restype = ctypes.c_char_p
         for name in EXPORTED:
@@ -378,3 +382,51 @@ def wait_selftest(limit_us: int = 20000, stream=None):
     _check(lib().b200_wait_selftest(_dptr(status), int(limit_us), _stream(stream)),
            "b200_wait_selftest")
     return [int(x) for x in status.cpu()]
+
+
+# ----------------------------------------------------------------- GEMM (tcgen05)
+GEMM_STORE_BF16, GEMM_RED_F32 = 0, 1
+
+
+def gemm(a, b, out=None, mode: int = GEMM_STORE_BF16, c_ptr: Optional[int] = None,
+         ldc: Optional[int] = None, status=None, stream=None):
+    """a [M, K] bf16 (row stride a.stride(0)) times b [N, K] bf16 (row stride b.stride(0))
+    transposed.  mode GEMM_STORE_BF16: out bf16 [M, N] = a @ b.T; GEMM_RED_F32: out f32
+    [M, N] += a @ b.T (c_ptr: a raw device address instead, e.g. a peer's buffer)."""
+    import torch
+    m, k = a.shape
+    n = b.shape[0]
+    if out is None and c_ptr is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
+    cp = c_ptr if c_ptr is not None else out.data_ptr()
+    if ldc is None:
+        ldc = out.stride(0)
+    _check(lib().b200_gemm(_dptr(a), a.stride(0), _dptr(b), b.stride(0), cp, ldc, m, n, k, mode,
+                           _dptr(status), _stream(stream)), "b200_gemm")
+    return out
+
+
+def _ptr_array(ptrs):
+    arr = (ctypes.c_void_p * len(ptrs))(*[int(p) for p in ptrs])
+    return arr
+
+
+def gemm_scatter(a, b, owner_ptrs, src_slot: int, rows_per_owner: int, ldc: int, status=None,
+                 stream=None):
+    """b200_gemm_scatter: rows of a @ b.T (bf16) into their owners' slots (see the header)."""
+    m, k = a.shape
+    n = b.shape[0]
+    arr = _ptr_array(owner_ptrs)
+    _check(lib().b200_gemm_scatter(_dptr(a), a.stride(0), _dptr(b), b.stride(0), arr, len(owner_ptrs),
+                                   src_slot, rows_per_owner, ldc, m, n, k, _dptr(status),
+                                   _stream(stream)), "b200_gemm_scatter")
+
+
+def reduce_gather(slots, n_src: int, slot_rows: int, rows: int, cols: int, ld: int, dst_ptrs,
+                  dst_row0: int, dst_ld: int, stream=None):
+    """b200_reduce_gather_bf16: sum the first `rows` rows of n_src slots (slot_rows rows
+    apart) and broadcast them to dst_ptrs at row dst_row0."""
+    arr = _ptr_array(dst_ptrs)
+    _check(lib().b200_reduce_gather_bf16(_dptr(slots), n_src, slot_rows, rows, cols, ld, arr,
+                                         len(dst_ptrs), dst_row0, dst_ld, _stream(stream)),
+           "b200_reduce_gather_bf16")

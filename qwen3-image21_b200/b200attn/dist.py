@@ -8,8 +8,13 @@ Two ways the path is partitioned inside one node:
   CFG branches are two sequential forward calls (src/pipeline.rs:154-197).
 - **Head sharding** (>= 2048^2) — rank r owns heads [h0, h1): its to_q/to_k/to_v column
   slices, its slice of every layer's prefix cache, and rows [h0*D, h1*D) of to_out's input
-  dimension.  Attention is local; the to_out partial sums of all ranks are added by one
-  NCCL all-reduce per layer (the reference's to_out is src/transformer.rs:196).
+  dimension.  Attention is local; the to_out partial sums of all ranks are added either by
+  one NCCL all-reduce per layer after a cuBLAS GEMM (`out_proj_partial` +
+  `allreduce_sum_`), or by the out-projection GEMM itself (`ScatterOutProj`): its epilogue
+  stores every partial tile straight into the rank that owns those rows (a reduce-scatter
+  overlapped with the GEMM, over NVLink), and a second kernel sums each owner's slots and
+  broadcasts the rows.  (The
+  reference's to_out is src/transformer.rs:196.)
 
 torch.distributed (NCCL on GPUs, gloo in the CPU tests) is the plumbing.
 """
@@ -90,3 +95,63 @@ def head_sharded_attention_layer(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w
     partial = out_proj_partial(attn.reshape(b * t, hl * d), w_out, h0, h1, d)
     allreduce_sum_(partial, group)
     return partial.reshape(b, t, -1)
+
+
+class ScatterOutProj:
+    """Head-sharded to_out fused with the reduction of its partial sums across ranks.
+
+    Rows of the output are split into `world` equal blocks; rank q owns block q.  Per rank,
+    two sets (alternating calls) of two symmetric-memory buffers: `slots` bf16
+    [world * rows_per, hidden] (rank s's partial of this rank's block lands in slot s) and
+    `out` bf16 [world * rows_per, hidden] (the full result).  A call:
+      b200_gemm_scatter: attn_local · w_cols^T, each tile stored into its owner's slot for
+                         this rank (plain stores over NVLink as tiles finish)
+      barrier (every slot written)
+      b200_reduce_gather_bf16: this rank sums its block's slots in a fixed order and writes
+                         the bf16 rows into every rank's `out`
+      barrier (every block written)
+    and returns this rank's `out` [T, hidden].  Alternating the buffer sets makes a leading
+    barrier unnecessary: the previous use of a set ended before the previous call's last
+    barrier, which every rank has passed.  The returned view stays valid until the call
+    after next.  Barriers time out after `timeout_ms`.
+    """
+
+    def __init__(self, rows: int, hidden: int, device, group=None, timeout_ms: int = 10000):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rows_per = -(-rows // self.world)
+        self.rows, self.hidden, self.timeout_ms = rows, hidden, timeout_ms
+        self.sets = []
+        for _ in range(2):
+            slots = symm_mem.empty(self.world * self.rows_per, hidden, dtype=torch.bfloat16,
+                                   device=device)
+            out = symm_mem.empty(self.world * self.rows_per, hidden, dtype=torch.bfloat16,
+                                 device=device)
+            h_slots = symm_mem.rendezvous(slots, group)
+            h_out = symm_mem.rendezvous(out, group)
+            self.sets.append(dict(slots=slots, out=out, h=h_out,
+                                  slot_ptrs=[int(p) for p in h_slots.buffer_ptrs],
+                                  out_ptrs=[int(p) for p in h_out.buffer_ptrs]))
+        self.calls = 0
+
+    def __call__(self, attn_local, w_out, h0: int, h1: int, head_dim: int = 128, status=None):
+        import b200attn
+        t = attn_local.shape[0]
+        if t > self.rows or w_out.shape[0] != self.hidden:
+            raise ValueError("shape does not fit the buffers")
+        st = self.sets[self.calls % 2]
+        self.calls += 1
+        w_cols = w_out[:, h0 * head_dim:h1 * head_dim]
+        b200attn.gemm_scatter(attn_local, w_cols, st["slot_ptrs"], self.rank, self.rows_per,
+                              self.hidden, status=status)
+        st["h"].barrier(channel=0, timeout_ms=self.timeout_ms)
+        r0 = self.rank * self.rows_per
+        mine = max(0, min(self.rows_per, t - r0))
+        b200attn.reduce_gather(st["slots"], self.world, self.rows_per, mine, self.hidden,
+                               self.hidden, st["out_ptrs"], r0, self.hidden)
+        st["h"].barrier(channel=0, timeout_ms=self.timeout_ms)
+        return st["out"][:t]

@@ -15,10 +15,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "b200attn", "libb200attn.so")
-SOURCES = ["attn_fwd.cu", "block_ops.cu", "dequant.cu", "host_layout.cpp"]
+SOURCES = ["attn_fwd.cu", "block_ops.cu", "dequant.cu", "gemm.cu", "host_layout.cpp"]
 HEADERS = ["ptx.cuh", os.path.join("..", "..", "include", "b200_attn.h"),
            os.path.join("..", "..", "include", "b200_block_ops.h"),
-           os.path.join("..", "..", "include", "b200_gguf.h")]
+           os.path.join("..", "..", "include", "b200_gguf.h"),
+           os.path.join("..", "..", "include", "b200_gemm.h")]
 
 
 def nvcc() -> str:

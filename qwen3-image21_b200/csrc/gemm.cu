@@ -1,0 +1,509 @@
+// gemm.cu — C = A · Bᵀ on tcgen05 with an epilogue that can reduce across GPUs.
+//
+// A [M, K] and B [N, K] are bf16, K-major (B is a Linear's weight [out, in]); the product
+// accumulates in f32 in TMEM.  The epilogue stores bf16, or adds f32 into a buffer with
+// `red.global.add` (a local buffer or another GPU's, through a peer pointer), or scatters
+// bf16 rows to the GPU that owns them (plain stores over NVLink into that GPU's slot for
+// this GPU).  The scatter is the out-projection of head-sharded attention fused with the
+// reduce-scatter of its partial sums: a GPU's partial tile leaves for its owner as soon as
+// it is computed; b200_reduce_gather_bf16 then sums each owner's slots and broadcasts.
+//
+// Structure: persistent CTAs (one per SM), 128 x 256 output tiles in n-fastest order (the
+// CTAs working on one row block share its A tiles in L2), 64-deep K steps.
+//   warp 0      TMA producer: A and B tiles into a 4-stage ring (no multicast)
+//   warp 1      MMA issuer: 4 x tcgen05.mma M128 N256 K16 per K step
+//   warp 2      TMEM allocator: 2 x 256 columns, the accumulator of the current tile and
+//               of the next one, so a tile's epilogue overlaps the next tile's MMAs
+//   warps 4-7   epilogue: TMEM -> registers -> a swizzled 128-row x 128-byte staging tile
+//               in shared memory (32 f32 or 64 bf16 columns) -> 16-byte vectors along rows
+//               (8 lanes cover one row's 128 contiguous bytes), so global / NVLink traffic
+//               leaves in full segments.
+// Every wait is bounded (ptx.cuh); a wait that runs out records a status code and the CTA
+// unwinds.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "../../include/b200_attn.h"
+#include "../../include/b200_gemm.h"
+#include "ptx.cuh"
+
+namespace b200 {
+namespace {
+
+constexpr int kGM = 128;                     // tile rows
+constexpr int kGN = 256;                     // tile columns
+constexpr int kGK = 64;                      // K per stage (one 128-byte swizzle span)
+constexpr int kGStages = 4;
+constexpr int kATileBytes = kGM * kGK * 2;   // 16 KiB
+constexpr int kBTileBytes = kGN * kGK * 2;   // 32 KiB
+constexpr int kStageBytes = kATileBytes + kBTileBytes;
+constexpr int kStageSmem = kGStages * kStageBytes;          // 192 KiB
+constexpr int kEpiChunk = 32;                                // columns per epilogue pass
+constexpr int kEpiSmem = kGM * kEpiChunk * 4;                // 16 KiB staging tile
+constexpr int kGBarOff = kStageSmem + kEpiSmem;
+constexpr int kGSmemBytes = kGBarOff + 256 + 1024;           // barriers + alignment slack
+constexpr int kGThreads = 256;
+constexpr uint32_t kGTmemCols = 512;                         // 2 accumulators x 256
+
+constexpr int kMaxOwners = 8;
+
+struct GemmParams {
+  int32_t M, N, K;
+  int32_t tiles_n, tiles;
+  int32_t mode;        // B200_GEMM_STORE_BF16 / _RED_F32 / _SCATTER_BF16
+  int64_t ldc;         // elements between rows of C
+  void* C;
+  int32_t* status;
+  // B200_GEMM_SCATTER_BF16: row m goes to owner q = m / rows_per_owner, into slot
+  // `src_slot` of owner q's buffer: peers[q] + (src_slot * rows_per_owner + m - q *
+  // rows_per_owner) * ldc.
+  void* peers[kMaxOwners];
+  int32_t rows_per_owner, src_slot;
+};
+
+struct ReduceGatherDst {
+  void* ptr[kMaxOwners];
+  int32_t n;
+  int64_t row0, ld8;
+};
+
+__device__ __forceinline__ uint32_t gemm_pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a),
+               "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+
+__device__ __forceinline__ void gemm_error(const GemmParams& p, volatile int* abort_flag, int code) {
+  *abort_flag = 1;
+  if (p.status) atomicCAS(p.status, 0, code);
+}
+
+__global__ void __launch_bounds__(kGThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* stage_tile = reinterpret_cast<float*>(smem + kStageSmem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGBarOff);
+  uint64_t* full = bars;                    // [kGStages]
+  uint64_t* empty = bars + kGStages;        // [kGStages]
+  uint64_t* acc_full = bars + 2 * kGStages; // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(acc_empty + 3);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nk = (p.K + kGK - 1) / kGK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 4 * 32);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, kGTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_a);
+      tma_prefetch_desc(&tm_b);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / p.tiles_n) * kGM;
+        const int n0 = (tile % p.tiles_n) * kGN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kGStages;
+          const uint32_t ph = (it / kGStages) & 1;
+          if (!mbar_wait(empty + s, ph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * kStageBytes;
+          mbar_expect_tx(full + s, kStageBytes);
+          tma_load_2d(sa, &tm_a, full + s, kb * kGK, m0);
+          tma_load_2d(sa + kATileBytes, &tm_b, full + s, kb * kGK, n0);
+        }
+      }
+      if (!ok) {
+        gemm_error(p, abort_flag, 1);
+        // Let issued copies land before the shared memory is released.
+        for (int s = 0; s < kGStages; ++s) mbar_wait(full + s, 0);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kGM, kGN, 0, 0);
+      const uint64_t d0 = smem_desc(smem_addr(smem), 16, 1024);
+      const uint32_t hi = static_cast<uint32_t>(d0 >> 32);
+      const uint32_t lo0 = static_cast<uint32_t>(d0);
+      uint32_t it = 0;
+      int lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, ++lt) {
+        const int ab = lt & 1;
+        const uint32_t aph = (lt >> 1) & 1;
+        if (!mbar_wait(acc_empty + ab, aph ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + ab * kGN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kGStages;
+          const uint32_t ph = (it / kGStages) & 1;
+          if (!mbar_wait(full + s, ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = lo0 + ((s * kStageBytes) >> 4);
+          const uint32_t b = a + (kATileBytes >> 4);
+          // K step kk: 16 columns = 32 bytes further inside the 128-byte swizzle span
+          mma_ss_off<0, 0>(d, a, hi, b, hi, idesc, kb > 0 ? 1u : 0u);
+          mma_ss_off<2, 2>(d, a, hi, b, hi, idesc, 1u);
+          mma_ss_off<4, 4>(d, a, hi, b, hi, idesc, 1u);
+          mma_ss_off<6, 6>(d, a, hi, b, hi, idesc, 1u);
+          mma_commit(empty + s);
+        }
+        if (!ok) break;
+        mma_commit(acc_full + ab);
+      }
+      if (!ok) gemm_error(p, abort_flag, 2);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;                 // TMEM lane quadrant of this warp
+    const int trow = q * 32 + lane;         // this thread's row of the tile
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    // staging tile: row r holds 32 f32 = 8 chunks of 16 bytes, chunk j at (j ^ (r & 7))
+    float4* st_row = reinterpret_cast<float4*>(stage_tile) + trow * 8;
+    const int sub = lane & 7;               // 16-byte chunk this lane moves in a pass
+    int lt = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++lt) {
+      const int ab = lt & 1;
+      const uint32_t aph = (lt >> 1) & 1;
+      if (!mbar_wait(acc_full + ab, aph, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int m0 = (tile / p.tiles_n) * kGM;
+      const int n0 = (tile % p.tiles_n) * kGN;
+      if (p.mode == B200_GEMM_RED_F32) {
+        // f32 red-add: 32 columns per pass, 4 f32 (16 bytes) per lane.
+        for (int c = 0; c < kGN / kEpiChunk; ++c) {
+          const int col0 = n0 + c * kEpiChunk;
+          if (col0 >= p.N) break;  // same for every thread of the tile
+          uint32_t r[32];
+          tmem_ld32(tmem_base + lane_off + ab * kGN + c * kEpiChunk, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            st_row[j ^ (trow & 7)] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          __syncwarp();
+          // This warp's 32 rows, 4 per pass: lane -> row (lane / 8), chunk (lane % 8).
+#pragma unroll
+          for (int pass = 0; pass < 8; ++pass) {
+            const int rr = q * 32 + pass * 4 + (lane >> 3);
+            const int m = m0 + rr;
+            const float4 v =
+                reinterpret_cast<const float4*>(stage_tile)[rr * 8 + (sub ^ (rr & 7))];
+            if (m < p.M)
+              red_add_v4(static_cast<float*>(p.C) + static_cast<int64_t>(m) * p.ldc + col0 + sub * 4,
+                         v.x, v.y, v.z, v.w);
+          }
+          __syncwarp();
+        }
+      } else {
+        // bf16 store / scatter: 64 columns per pass (two TMEM loads), 8 bf16 (16 bytes) per
+        // lane, so each row leaves as one 128-byte segment.
+        for (int c = 0; c < kGN / 64; ++c) {
+          const int col0 = n0 + c * 64;
+          if (col0 >= p.N) break;  // same for every thread of the tile
+          const bool two = col0 + 32 < p.N;
+          uint32_t r[32], w[32];
+          tmem_ld32(tmem_base + lane_off + ab * kGN + c * 64, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) w[i] = gemm_pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+          if (two) {
+            tmem_ld32(tmem_base + lane_off + ab * kGN + c * 64 + 32, r);
+            tmem_wait_ld();
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            w[16 + i] = two ? gemm_pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])) : 0u;
+          uint4* st4 = reinterpret_cast<uint4*>(stage_tile) + trow * 8;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            st4[j ^ (trow & 7)] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int pass = 0; pass < 8; ++pass) {
+            const int rr = q * 32 + pass * 4 + (lane >> 3);
+            const int m = m0 + rr;
+            const uint4 v = reinterpret_cast<const uint4*>(stage_tile)[rr * 8 + (sub ^ (rr & 7))];
+            const int col = col0 + sub * 8;
+            if (m < p.M && col < p.N) {
+              __nv_bfloat16* dst;
+              if (p.mode == B200_GEMM_STORE_BF16) {
+                dst = static_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(m) * p.ldc + col;
+              } else {  // scatter: the owner's slot for this rank, over NVLink for others
+                const int owner = m / p.rows_per_owner;
+                const int64_t row = static_cast<int64_t>(p.src_slot) * p.rows_per_owner + (m - owner * p.rows_per_owner);
+                dst = static_cast<__nv_bfloat16*>(p.peers[owner]) + row * p.ldc + col;
+              }
+              *reinterpret_cast<uint4*>(dst) = v;
+            }
+          }
+          __syncwarp();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty + ab);
+    }
+    if (!ok) gemm_error(p, abort_flag, 3);
+    // Writes into other GPUs' memory are performed at system scope before the CTA exits,
+    // so a barrier after the kernel orders every GPU's reads after them.
+    if (p.mode != B200_GEMM_STORE_BF16) __threadfence_system();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kGTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 gemm_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 2-D map over a bf16 row-major matrix [rows, cols] with `ld` elements between rows; box
+// 64 columns x box_rows rows, 128-byte swizzle, zero fill outside.
+int make_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                uint32_t box_rows) {
+  auto fn = gemm_encode_fn();
+  if (!fn) return B200_ERR_CUDA;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kGK), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B200_OK : B200_ERR_CUDA;
+}
+
+int gemm_sms() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+int ensure_gemm_attrs() {
+  static std::mutex mu;
+  static int done_dev = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B200_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done_dev == dev) return B200_OK;
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0) return B200_ERR_UNSUPPORTED;
+  if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kGSmemBytes) != cudaSuccess)
+    return B200_ERR_CUDA;
+  done_dev = dev;
+  return B200_OK;
+}
+
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+namespace b200 {
+namespace {
+
+int launch_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
+                int32_t m, int32_t n, int32_t k, int32_t mode, int32_t* status,
+                cudaStream_t stream, void* const* peers, int32_t n_owners,
+                int32_t rows_per_owner, int32_t src_slot);
+
+}  // namespace
+}  // namespace b200
+
+extern "C" int b200_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c,
+                         int64_t ldc, int32_t m, int32_t n, int32_t k, int32_t mode,
+                         int32_t* status, b200_stream_t stream) {
+  if (mode != B200_GEMM_STORE_BF16 && mode != B200_GEMM_RED_F32) return B200_ERR_INVALID;
+  return launch_gemm(a, lda, b, ldb, c, ldc, m, n, k, mode, status,
+                     static_cast<cudaStream_t>(stream), nullptr, 0, 0, 0);
+}
+
+extern "C" int b200_gemm_scatter(const void* a, int64_t lda, const void* b, int64_t ldb,
+                                 void* const* owner_bufs, int32_t n_owners, int32_t src_slot,
+                                 int32_t rows_per_owner, int64_t ldc, int32_t m, int32_t n,
+                                 int32_t k, int32_t* status, b200_stream_t stream) {
+  if (!owner_bufs || n_owners < 1 || n_owners > kMaxOwners) return B200_ERR_INVALID;
+  if (src_slot < 0 || src_slot >= n_owners || rows_per_owner <= 0) return B200_ERR_INVALID;
+  if (static_cast<int64_t>(rows_per_owner) * n_owners < m) return B200_ERR_INVALID;
+  for (int i = 0; i < n_owners; ++i)
+    if (!owner_bufs[i] || (reinterpret_cast<uintptr_t>(owner_bufs[i]) & 15u)) return B200_ERR_INVALID;
+  return launch_gemm(a, lda, b, ldb, owner_bufs[0], ldc, m, n, k, B200_GEMM_SCATTER_BF16, status,
+                     static_cast<cudaStream_t>(stream), owner_bufs, n_owners, rows_per_owner,
+                     src_slot);
+}
+
+namespace b200 {
+namespace {
+
+int launch_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
+                int32_t m, int32_t n, int32_t k, int32_t mode, int32_t* status,
+                cudaStream_t stream, void* const* peers, int32_t n_owners,
+                int32_t rows_per_owner, int32_t src_slot) {
+  if (m < 0 || n < 0 || k < 0) return B200_ERR_INVALID;
+  if (m == 0 || n == 0) return B200_OK;
+  if (!a || !b || !c || !al16(a) || !al16(b) || !al16(c)) return B200_ERR_INVALID;
+  // TMA: 16-byte row strides; epilogue: 32-column chunks, 8- (bf16) or 16-byte vectors.
+  if (k == 0 || k % 8 != 0 || lda < k || ldb < k || lda % 8 != 0 || ldb % 8 != 0)
+    return B200_ERR_INVALID;
+  if (n % 32 != 0 || ldc < n || ldc % 8 != 0) return B200_ERR_INVALID;
+  int rc = ensure_gemm_attrs();
+  if (rc != B200_OK) return rc;
+  CUtensorMap ma{}, mb{};
+  if ((rc = make_map_2d(&ma, a, m, k, lda, kGM)) != B200_OK) return rc;
+  if ((rc = make_map_2d(&mb, b, n, k, ldb, kGN)) != B200_OK) return rc;
+  GemmParams p{};
+  p.M = m;
+  p.N = n;
+  p.K = k;
+  p.tiles_n = (n + kGN - 1) / kGN;
+  const int64_t tiles = static_cast<int64_t>((m + kGM - 1) / kGM) * p.tiles_n;
+  if (tiles > 0x7fffffff) return B200_ERR_INVALID;
+  p.tiles = static_cast<int32_t>(tiles);
+  p.mode = mode;
+  p.ldc = ldc;
+  p.C = c;
+  p.status = status;
+  for (int i = 0; i < n_owners; ++i) p.peers[i] = peers[i];
+  p.rows_per_owner = rows_per_owner;
+  p.src_slot = src_slot;
+  const int grid = static_cast<int>(tiles < gemm_sms() ? tiles : gemm_sms());
+  gemm_kernel<<<grid, kGThreads, kGSmemBytes, stream>>>(ma, mb, p);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
+
+// Sum of a row block's slots, broadcast as bf16: thread -> 8 columns of one row.
+__global__ void __launch_bounds__(256) reduce_gather_kernel(const uint4* slots, int32_t n_src,
+                                                            int32_t rows, int32_t c8,
+                                                            int64_t ld8, int64_t slot_stride8,
+                                                            ReduceGatherDst dst) {
+  const int64_t total = static_cast<int64_t>(rows) * c8;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / c8;
+    const int c = static_cast<int>(i - r * c8);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < n_src; ++s) {  // fixed order: the sum does not depend on timing
+      const uint4 u = slots[s * slot_stride8 + r * ld8 + c];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[2 * e] += __uint_as_float(w[e] << 16);
+        acc[2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+      }
+    }
+    uint4 o;
+    uint32_t ow[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __nv_bfloat162 v = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+      ow[e] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    o = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    const int64_t drow = dst.row0 + r;
+    for (int d = 0; d < dst.n; ++d) static_cast<uint4*>(dst.ptr[d])[drow * dst.ld8 + c] = o;
+  }
+  __threadfence_system();
+}
+
+}  // namespace
+}  // namespace b200
+
+extern "C" int b200_reduce_gather_bf16(const void* slots, int32_t n_src, int32_t slot_rows,
+                                       int32_t rows, int32_t cols, int64_t ld,
+                                       void* const* dst_bufs, int32_t n_dst, int64_t dst_row0,
+                                       int64_t dst_ld, b200_stream_t stream) {
+  if (!slots || n_src < 1 || rows < 0 || slot_rows < rows || cols <= 0 || cols % 8 != 0 ||
+      ld < cols || ld % 8 != 0)
+    return B200_ERR_INVALID;
+  if (!dst_bufs || n_dst < 1 || n_dst > kMaxOwners || dst_row0 < 0 || dst_ld < cols || dst_ld % 8 != 0)
+    return B200_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(slots) & 15u) return B200_ERR_INVALID;
+  ReduceGatherDst dst{};
+  for (int i = 0; i < n_dst; ++i) {
+    if (!dst_bufs[i] || (reinterpret_cast<uintptr_t>(dst_bufs[i]) & 15u)) return B200_ERR_INVALID;
+    dst.ptr[i] = dst_bufs[i];
+  }
+  dst.n = n_dst;
+  dst.row0 = dst_row0;
+  dst.ld8 = dst_ld / 8;
+  if (rows == 0) return B200_OK;
+  const int64_t total = static_cast<int64_t>(rows) * (cols / 8);
+  const int64_t want = (total + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(gemm_sms()) * 8;
+  reduce_gather_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0,
+                         static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(slots), n_src, rows, cols / 8, ld / 8,
+      static_cast<int64_t>(slot_rows) * (ld / 8), dst);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}

@@ -1,4 +1,4 @@
-// ptx.cuh — inline-PTX wrappers for the sm_100a features the attention kernel uses:
+// ptx.cuh — inline-PTX wrappers for the sm_100a features the attention and GEMM kernels use:
 // mbarriers (bounded waits), TMA tiled loads (no multicast), tcgen05 TMEM allocation,
 // tcgen05.mma (kind::f16, A from shared memory or from TMEM), tcgen05.commit and
 // tcgen05.ld / tcgen05.st (32x32b shape).
@@ -90,6 +90,16 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_addr(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2),
       "r"(c3)
+      : "memory");
+}
+
+// 2-D tiled load (coordinates: inner, outer), as tma_load_4d.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1)
       : "memory");
 }
 

@@ -18,7 +18,7 @@ GOLDEN = os.path.join(ROOT, "tests", "golden")
 
 def declared_functions():
     names = set()
-    for hdr in ("b200_attn.h", "b200_block_ops.h", "b200_gguf.h"):
+    for hdr in ("b200_attn.h", "b200_block_ops.h", "b200_gguf.h", "b200_gemm.h"):
         src = open(os.path.join(ROOT, "include", hdr)).read()
         src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
         names |= set(re.findall(r"\b(b200_[a-z0-9_]+)\s*\(", src))

@@ -73,3 +73,51 @@ def test_head_sharded_layer_matches_single_gpu(tmp_path):
     mp.spawn(_rank, args=(2, _free_port(), str(result)), nprocs=2, join=True)
     rel = float(result.read_text())
     assert rel <= 5e-3, rel
+
+
+def _rank_fused(rank, world, port, result_path):
+    import torch
+    import torch.distributed as dist
+
+    import b200attn
+    from b200attn import dist as bdist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, device_id=dev)
+    try:
+        T, H, hidden = 1000, 8, 1024
+        g = torch.Generator().manual_seed(17)
+        attn = torch.randn(T, H * 128, generator=g).bfloat16().to(dev)
+        w_out = (0.02 * torch.randn(hidden, H * 128, generator=g)).bfloat16().to(dev)
+        h0, h1 = bdist.head_shard(H, world, rank)
+        fused = bdist.ScatterOutProj(T, hidden, dev)
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+        for _ in range(2):   # the second call must start from a zeroed buffer again
+            out = fused(attn[:, h0 * 128:h1 * 128].contiguous(), w_out, h0, h1, status=st)
+        torch.cuda.synchronize()
+        want = attn.float() @ w_out.float().t()
+        rel = float((out.float() - want).norm() / want.norm())
+        worst = bdist.max_over_ranks(rel, device=dev)
+        bad = bdist.max_over_ranks(float(st.item()), device=dev)
+        if rank == 0:
+            with open(result_path, "w") as f:
+                f.write(f"{worst} {bad}")
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_scatter_fused_out_proj_matches_single_gpu(tmp_path):
+    """The to_out GEMM whose epilogue reduce-scatters over NVLink, then the owners' sum and
+    broadcast: every rank ends with the full projection of all heads."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    result = tmp_path / "fused.txt"
+    mp.spawn(_rank_fused, args=(2, _free_port(), str(result)), nprocs=2, join=True)
+    worst, bad = map(float, result.read_text().split())
+    assert bad == 0
+    assert worst < 5e-3, worst    # bf16 partials summed in f32, rounded to bf16
