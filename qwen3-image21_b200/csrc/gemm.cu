@@ -8,8 +8,8 @@
 // reduce-scatter of its partial sums: a GPU's partial tile leaves for its owner as soon as
 // it is computed; b200_reduce_gather_bf16 then sums each owner's slots and broadcasts.
 //
-// Structure: persistent CTAs (one per SM), 128 x 256 output tiles in n-fastest order (the
-// CTAs working on one row block share its A tiles in L2), 64-deep K steps.
+// Structure: persistent CTAs (one per SM), 128 x 256 output tiles in a grouped raster
+// (tile_coords), 64-deep K steps.
 //   warp 0      TMA producer: A and B tiles into a 4-stage ring (no multicast)
 //   warp 1      MMA issuer: 4 x tcgen05.mma M128 N256 K16 per K step
 //   warp 2      TMEM allocator: 2 x 256 columns, the accumulator of the current tile and
@@ -52,9 +52,11 @@ constexpr uint32_t kGTmemCols = 512;                         // 2 accumulators x
 
 constexpr int kMaxOwners = 8;
 
+constexpr int kGroupM = 8;  // row blocks per raster group
+
 struct GemmParams {
   int32_t M, N, K;
-  int32_t tiles_n, tiles;
+  int32_t tiles_m, tiles_n, tiles;
   int32_t mode;        // B200_GEMM_STORE_BF16 / _RED_F32 / _SCATTER_BF16
   int64_t ldc;         // elements between rows of C
   void* C;
@@ -83,6 +85,19 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
                : "memory");
 }
 
+
+// Grouped raster: tiles run in groups of kGroupM row blocks, row-block-fastest inside a
+// group, so the CTAs in flight share a few A row blocks and a band of B column blocks
+// (both stay in L2 even when B is larger than L2).
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& m0, int& n0) {
+  const int per_group = kGroupM * p.tiles_n;
+  const int g = t / per_group;
+  const int first = g * kGroupM;
+  const int gm = min(kGroupM, p.tiles_m - first);
+  const int local = t - g * per_group;
+  m0 = (first + local % gm) * kGM;
+  n0 = (local / gm) * kGN;
+}
 
 __device__ __forceinline__ void gemm_error(const GemmParams& p, volatile int* abort_flag, int code) {
   *abort_flag = 1;
@@ -138,8 +153,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / p.tiles_n) * kGM;
-        const int n0 = (tile % p.tiles_n) * kGN;
+        int m0, n0;
+        tile_coords(p, tile, m0, n0);
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % kGStages;
           const uint32_t ph = (it / kGStages) & 1;
@@ -218,8 +233,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
         break;
       }
       tc_fence_after();
-      const int m0 = (tile / p.tiles_n) * kGM;
-      const int n0 = (tile % p.tiles_n) * kGN;
+      int m0, n0;
+      tile_coords(p, tile, m0, n0);
       if (p.mode == B200_GEMM_RED_F32) {
         // f32 red-add: 32 columns per pass, 4 f32 (16 bytes) per lane.
         for (int c = 0; c < kGN / kEpiChunk; ++c) {
@@ -427,7 +442,8 @@ int launch_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c,
   p.N = n;
   p.K = k;
   p.tiles_n = (n + kGN - 1) / kGN;
-  const int64_t tiles = static_cast<int64_t>((m + kGM - 1) / kGM) * p.tiles_n;
+  p.tiles_m = (m + kGM - 1) / kGM;
+  const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
   if (tiles > 0x7fffffff) return B200_ERR_INVALID;
   p.tiles = static_cast<int32_t>(tiles);
   p.mode = mode;
