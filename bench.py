@@ -415,10 +415,11 @@ def main():
 def run_head_sharded(args, cfg, rank, world, dev):
     """Config 4: each rank runs the attention of its 32/N heads and its share of to_out; a
     step is one block (strong scaling).  Two ways to sum the to_out partials are timed
-    back to back: the fused one (value) — the tcgen05 out-projection GEMM whose epilogue
-    stores every partial tile into the rank owning its rows, then the owners' sum and
-    broadcast (ScatterOutProj) — and the baseline, a cuBLAS GEMM followed by an NCCL
-    all-reduce.  On one GPU both are a plain GEMM."""
+    back to back: the fused one — the tcgen05 out-projection GEMM whose epilogue stores
+    every partial tile into the rank owning its rows, then the owners' sum and broadcast
+    (ScatterOutProj) — and a cuBLAS GEMM followed by an NCCL all-reduce.  `value` is the
+    path dist.prefer_fused_out_proj picks for this rank count (both are reported).  On one
+    GPU the step is the attention and a plain tcgen05 GEMM."""
     import torch
     import torch.distributed as dist
 
@@ -454,6 +455,7 @@ def run_head_sharded(args, cfg, rank, world, dev):
                           "owner sum / broadcast kernel")
         except RuntimeError as e:
             fused_note = f"no symmetric memory ({e}); fused path = NCCL path"
+    use_fused = world == 1 or (fused is not None and bdist.prefer_fused_out_proj(world))
     out_bf16 = torch.empty(T, hidden, dtype=torch.bfloat16, device=dev)
 
     def attention(mark=None):
@@ -509,8 +511,9 @@ def run_head_sharded(args, cfg, rank, world, dev):
     ms_nccl = timed(step_nccl, args.steps)
     if int(status.item()) != 0:
         raise RuntimeError(f"device wait ran out during the bench (status {int(status.item())})")
-    ms_step = bdist.max_over_ranks(ms_fused, device=dev)
+    ms_fused = bdist.max_over_ranks(ms_fused, device=dev)
     ms_nccl = bdist.max_over_ranks(ms_nccl, device=dev)
+    ms_step = ms_fused if use_fused else ms_nccl
     attn_ms = bdist.max_over_ranks(attn_ms, device=dev)
     attn_flops = 4.0 * HEADS * T * (P + T) * HEAD_DIM
     proj_flops = 2.0 * T * HEADS * HEAD_DIM * hidden
@@ -526,16 +529,20 @@ def run_head_sharded(args, cfg, rank, world, dev):
             "data": "synthetic (seeded N(0,1) q/k/v and prefix cache, N(0,0.02) to_out)",
             "config": {"workload": cfg["name"] + ", one block per step", "T": T, "P": P,
                        "heads_per_gpu": hl, "head_dim": HEAD_DIM, "hidden": hidden,
-                       "parallelism": f"heads/{world}; to_out partials summed by {fused_note}",
+                       "parallelism": (f"heads/{world}; to_out partials summed by "
+                                       + (fused_note if use_fused else
+                                          "cuBLAS + NCCL all-reduce (faster than the fused "
+                                          "path at this rank count)")),
                        "l2": "inputs exceed L2"},
             "nccl_path": {"ms_per_step": ms_nccl,
                           "value": (attn_flops + proj_flops) / (ms_nccl / 1e3) / 1e12,
                           "how": "cuBLAS to_out partial + NCCL all-reduce (bf16)"},
+            "fused_path": {"ms_per_step": ms_fused, "how": fused_note},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": None, "kernel": "joint_attn_kernel",
                          "peak_source": f"{src} bf16_tflops_sustained", "launch_ms": attn_ms},
             "cpu_baseline": None, "e2e": None, "clocks": clocks.summary(),
-            "gpu_launches": args.steps * (4 if world > 1 else 3),
+            "gpu_launches": args.steps * (4 if world > 1 and use_fused else 2 if world > 1 else 3),
         }
         print(json.dumps(line), flush=True)
     del fused

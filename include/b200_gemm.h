@@ -39,6 +39,7 @@ extern "C" {
 #define B200_GEMM_STORE_BF16 0    /* C bf16 = A·Bᵀ                                       */
 #define B200_GEMM_RED_F32 1       /* C f32 += A·Bᵀ (red.global.add; C may be a peer's)    */
 #define B200_GEMM_SCATTER_BF16 2  /* internal: the epilogue of b200_gemm_scatter          */
+#define B200_GEMM_QKV 3           /* internal: the epilogue of b200_qkv_norm_rope_gemm    */
 #define B200_GEMM_MAX_OWNERS 8
 
 int b200_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
@@ -65,6 +66,23 @@ int b200_gemm_scatter(const void* a, int64_t lda, const void* b, int64_t ldb,
 int b200_reduce_gather_bf16(const void* slots, int32_t n_src, int32_t slot_rows, int32_t rows,
                             int32_t cols, int64_t ld, void* const* dst_bufs, int32_t n_dst,
                             int64_t dst_row0, int64_t dst_ld, b200_stream_t stream);
+
+/*
+ * The Q/K/V projections of one attention layer with the Q/K RMSNorm and RoPE in the
+ * GEMM's epilogue: x [B * T, in_features] bf16 (row stride ldx) times w_qkv
+ * [3 * H * 128, in_features] bf16 (to_q, to_k, to_v stacked) transposed, then
+ *   q_rot, k_rot: head-major [B, H, T, 128] bf16, RMSNorm (norm_q_w / norm_k_w, eps) then
+ *                 interleaved RoPE with pe rows pe + b * pe_batch_stride + t * 128 (f32)
+ *   v:            token-major [B, T, H * 128] bf16
+ * — the inputs of b200_joint_attention.  Replaces src/transformer.rs:173-185 (to_q / to_k
+ * / to_v, reshape, norm_q / norm_k, transpose, apply_rope) for a cached step; the
+ * unfused equivalent is three GEMMs and b200_qk_norm_rope.  H must be even.
+ */
+int b200_qkv_norm_rope_gemm(const void* x, int64_t ldx, const void* w_qkv, int32_t batch,
+                            int32_t tokens, int32_t heads, int32_t in_features,
+                            const float* norm_q_w, const float* norm_k_w, float eps,
+                            const float* pe, int64_t pe_batch_stride, void* q_rot,
+                            void* k_rot, void* v, int32_t* status, b200_stream_t stream);
 
 #ifdef __cplusplus
 }

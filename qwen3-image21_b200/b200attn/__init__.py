@@ -34,7 +34,7 @@ EXPORTED = (
     "b200_strerror", "b200_abi_version",
     "b200_residual_adaln", "b200_swiglu",
     "b200_dequant_q4_k", "b200_dequant_q6_k", "b200_wait_selftest", "b200_gemm",
-    "b200_gemm_scatter", "b200_reduce_gather_bf16",
+    "b200_gemm_scatter", "b200_reduce_gather_bf16", "b200_qkv_norm_rope_gemm",
 )
 
 
@@ -97,6 +97,8 @@ def lib() -> ctypes.CDLL:
         L.b200_gemm.argtypes = [vp, i64, vp, i64, vp, i64, i32, i32, i32, i32, vp, vp]
         L.b200_gemm_scatter.argtypes = [vp, i64, vp, i64, vp, i32, i32, i32, i64, i32, i32, i32, vp, vp]
         L.b200_reduce_gather_bf16.argtypes = [vp, i32, i32, i32, i32, i64, vp, i32, i64, i64, vp]
+        L.b200_qkv_norm_rope_gemm.argtypes = [vp, i64, vp, i32, i32, i32, i32, vp, vp, f32, vp, i64,
+                                              vp, vp, vp, vp, vp]
         L.b200_strerror.argtypes = [ctypes.c_int]
         L.b200_strerror.restype = ctypes.c_char_p
         for name in EXPORTED:
@@ -430,3 +432,25 @@ def reduce_gather(slots, n_src: int, slot_rows: int, rows: int, cols: int, ld: i
     _check(lib().b200_reduce_gather_bf16(_dptr(slots), n_src, slot_rows, rows, cols, ld, arr,
                                          len(dst_ptrs), dst_row0, dst_ld, _stream(stream)),
            "b200_reduce_gather_bf16")
+
+
+def qkv_norm_rope_gemm(x, w_qkv, batch: int, tokens: int, heads: int, norm_q_w, norm_k_w, pe,
+                       eps: float = 1e-6, q_rot=None, k_rot=None, v=None, status=None,
+                       stream=None):
+    """x bf16 [B*T, C] @ w_qkv[3*H*128, C]^T with the Q/K RMSNorm + RoPE in the epilogue ->
+    (q_rot, k_rot) head-major bf16 [B, H, T, 128] and v token-major bf16 [B, T, H, 128].
+    pe f32 [T, 128] (shared) or [B, T, 128] (one table per batch row)."""
+    import torch
+    dev = x.device
+    if q_rot is None:
+        q_rot = torch.empty((batch, heads, tokens, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    if k_rot is None:
+        k_rot = torch.empty((batch, heads, tokens, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    if v is None:
+        v = torch.empty((batch, tokens, heads, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    pe_bs = pe.shape[-2] * pe.shape[-1] if pe.dim() == 3 else 0
+    _check(lib().b200_qkv_norm_rope_gemm(_dptr(x), x.stride(0), _dptr(w_qkv), batch, tokens, heads,
+                                         x.shape[1], _dptr(norm_q_w), _dptr(norm_k_w), float(eps),
+                                         _dptr(pe), pe_bs, _dptr(q_rot), _dptr(k_rot), _dptr(v),
+                                         _dptr(status), _stream(stream)), "b200_qkv_norm_rope_gemm")
+    return q_rot, k_rot, v

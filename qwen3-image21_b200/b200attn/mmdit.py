@@ -174,18 +174,23 @@ class MMDiT:
     """The transformer on one GPU with bf16 weights (see module docstring)."""
 
     def __init__(self, cfg: MMDiTConfig, weights: dict, device="cuda", mlp_chunk_rows: int = 16384,
-                 weight_format: str = "bf16"):
+                 weight_format: str = "bf16", fused_qkv: bool = False):
         """weight_format "bf16" keeps the block linears in bf16; "q4_k_m" stores them as GGUF
         Q4_K / Q6_K super-blocks (llama.cpp's Q4_K_M rule) and dequantises each block's six
         matrices to a bf16 scratch right before its GEMMs.  The other weights (img_in,
         txt_in, timestep, modulation, norm_out, proj_out: 1 % of the parameters) stay
-        bf16 / f32 either way."""
+        bf16 / f32 either way.  fused_qkv: a cached step runs the Q/K/V projections with the
+        Q/K RMSNorm + RoPE in the GEMM epilogue (b200_qkv_norm_rope_gemm) and then the
+        attention kernel alone; otherwise (the default, 1.3 % faster at config 5 while the
+        tcgen05 GEMM runs the 12288-wide projection at ~90 % of cuBLAS) three cuBLAS GEMMs
+        and b200_attn_fwd."""
         import torch
         if weight_format not in ("bf16", "q4_k_m"):
             raise ValueError(f"unknown weight format {weight_format!r}")
         self.cfg, self.device = cfg, torch.device(device)
         self.mlp_chunk_rows = mlp_chunk_rows
         self.weight_format = weight_format
+        self.fused_qkv = fused_qkv
         dev = self.device
         bf = lambda n: weights[n].to(device=dev, dtype=torch.bfloat16).contiguous()
         f32 = lambda n: weights[n].to(device=dev, dtype=torch.float32).contiguous()
@@ -210,12 +215,17 @@ class MMDiT:
                 wgp=torch.cat([bf(p + "img_mlp.gate_layer.weight"),
                                bf(p + "img_mlp.proj.weight")], 0).contiguous(),
                 wmo=bf(p + "img_mlp.out.weight")))
+        h = cfg.hidden
+        for blk in self.blocks:  # [to_q ; to_k ; to_v] stacked: one GEMM for the fused path
+            blk["wqkv"] = torch.cat([blk.pop("wq"), blk.pop("wk"), blk.pop("wv")], 0).contiguous()
+            blk["wq"], blk["wk"], blk["wv"] = (blk["wqkv"][j * h:(j + 1) * h] for j in range(3))
         if weight_format == "q4_k_m":
             from b200attn import gguf as bq
             # reference names of the block linears (the fused gate_up is one GGUF tensor in
             # ComfyUI-style files, src/quantized_transformer.rs:160-166, output [gate; up])
             names = dict(wq="to_q", wk="to_k", wv="to_v", wo="to_out", wgp="gate_up", wmo="out")
             for i, blk in enumerate(self.blocks):
+                del blk["wqkv"]
                 for key, name in names.items():
                     w = blk.pop(key)
                     qtype = bq.q4_k_m_type(name, i, cfg.layers)
@@ -223,7 +233,8 @@ class MMDiT:
                     del w
         self._bufs = {}
         # When a list, every attention call of the block loop appends its (start, end) CUDA
-        # events (the b200_attn_fwd span: Q/K norm + RoPE prologue and attention kernel).
+        # events (the attention kernel; with fused_qkv off, the b200_attn_fwd span of Q/K
+        # norm + RoPE prologue and attention kernel).
         self.attn_marks = None
 
     # -- small helpers -------------------------------------------------------------
@@ -269,7 +280,12 @@ class MMDiT:
         if self.weight_format == "bf16":
             return blk
         out = dict(nq=blk["nq"], nk=blk["nk"])
-        for key in ("wq", "wk", "wv", "wo", "wgp", "wmo"):
+        h = self.cfg.hidden
+        wqkv = self._buf("dq_wqkv", (3 * h, h), torch.bfloat16)
+        for j, key in enumerate(("wq", "wk", "wv")):
+            out[key] = blk["q_" + key].dequant_into(wqkv[j * h:(j + 1) * h])
+        out["wqkv"] = wqkv
+        for key in ("wo", "wgp", "wmo"):
             ql = blk["q_" + key]
             out[key] = ql.dequant_into(self._buf("dq_" + key, ql.shape, torch.bfloat16))
         return out
@@ -278,8 +294,10 @@ class MMDiT:
         """HBM bytes of the block linears (the 99 % of the parameters they hold)."""
         total = 0
         for blk in self.blocks:
-            for key in ("wq", "wk", "wv", "wo", "wgp", "wmo"):
-                total += blk[key].numel() * 2 if key in blk else blk["q_" + key].nbytes()
+            if self.weight_format == "bf16":
+                total += sum(blk[k].numel() * 2 for k in ("wqkv", "wo", "wgp", "wmo"))
+            else:
+                total += sum(blk["q_" + k].nbytes() for k in ("wq", "wk", "wv", "wo", "wgp", "wmo"))
         return total
 
     def effective_weights(self, weights: dict) -> dict:
@@ -328,18 +346,32 @@ class MMDiT:
         b200attn.residual_adaln(x, None, None, scale1, y, rows_per_mod=R)      # norm1 of block 0
         for i in range(len(self.blocks)):
             blk = self.block_weights(i)
-            q = self._gemm(y, blk["wq"], "q").view(B, T, H, HEAD_DIM)
-            k = self._gemm(y, blk["wk"], "k").view(B, T, H, HEAD_DIM)
-            v = self._gemm(y, blk["wv"], "v").view(B, T, H, HEAD_DIM)
+            fused = self.fused_qkv and kv_out is None and row_limit is None and H % 2 == 0
+            if fused:   # projections + Q/K norm + RoPE in one GEMM, then the attention kernel
+                q_rot, k_rot, v = b200attn.qkv_norm_rope_gemm(
+                    y, blk["wqkv"], B, T, H, blk["nq"], blk["nk"], pe,
+                    q_rot=self._buf("q_rot", (B, H, T, HEAD_DIM), torch.bfloat16),
+                    k_rot=self._buf("k_rot", (B, H, T, HEAD_DIM), torch.bfloat16),
+                    v=self._buf("v", (B, T, H, HEAD_DIM), torch.bfloat16))
+            else:
+                q = self._gemm(y, blk["wq"], "q").view(B, T, H, HEAD_DIM)
+                k = self._gemm(y, blk["wk"], "k").view(B, T, H, HEAD_DIM)
+                v = self._gemm(y, blk["wv"], "v").view(B, T, H, HEAD_DIM)
             if self.attn_marks is not None:
                 ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 ev[0].record()
-            b200attn.attention_forward(
-                q, k, v, None if prefix is None else prefix.k[i],
-                None if prefix is None else prefix.v[i], blk["nq"], blk["nk"], pe, desc=desc,
-                out=attn, workspace=ws, row_limit=row_limit,
-                k_rot_out=None if kv_out is None else kv_out.k[i],
-                v_out=None if kv_out is None else kv_out.v[i])
+            if fused:
+                b200attn.joint_attention(
+                    q_rot, k_rot, v, None if prefix is None else prefix.k[i],
+                    None if prefix is None else prefix.v[i], desc=desc, out=attn,
+                    workspace=ws[:b200attn.SPLIT_WORKSPACE_BYTES])
+            else:
+                b200attn.attention_forward(
+                    q, k, v, None if prefix is None else prefix.k[i],
+                    None if prefix is None else prefix.v[i], blk["nq"], blk["nk"], pe, desc=desc,
+                    out=attn, workspace=ws, row_limit=row_limit,
+                    k_rot_out=None if kv_out is None else kv_out.k[i],
+                    v_out=None if kv_out is None else kv_out.v[i])
             if self.attn_marks is not None:
                 ev[1].record()
                 self.attn_marks.append(ev)

@@ -66,6 +66,19 @@ struct GemmParams {
   // rows_per_owner) * ldc.
   void* peers[kMaxOwners];
   int32_t rows_per_owner, src_slot;
+  // B200_GEMM_QKV: N = 3 * heads * 128 columns [q | k | v]; row m is token t = m % tokens
+  // of batch row b = m / tokens.  q and k get RMSNorm (norm_q / norm_k, eps) and RoPE (pe
+  // rows: pe + b * pe_bs + t * 128) and go head-major [B, H, T, 128] to q_out / k_out; v
+  // goes token-major [B, T, H * 128] to v_out.
+  int32_t heads, tokens;
+  const float* pe;
+  int64_t pe_bs;
+  const float* norm_q;
+  const float* norm_k;
+  float eps;
+  void* q_out;
+  void* k_out;
+  void* v_out;
 };
 
 struct ReduceGatherDst {
@@ -235,7 +248,71 @@ __global__ void __launch_bounds__(kGThreads, 1)
       tc_fence_after();
       int m0, n0;
       tile_coords(p, tile, m0, n0);
-      if (p.mode == B200_GEMM_RED_F32) {
+      const int hidden = p.heads * 128;
+      const int which = p.mode == B200_GEMM_QKV ? n0 / hidden : -1;
+      if (which == 0 || which == 1) {
+        // Q or K of two heads: RMSNorm over each head's 128 values (a first pass over TMEM
+        // for the sum of squares), then RoPE, bf16, head-major rows, 64 columns per pass.
+        const float* wn = which == 0 ? p.norm_q : p.norm_k;
+        __nv_bfloat16* dst_base = static_cast<__nv_bfloat16*>(which == 0 ? p.q_out : p.k_out);
+        const int m = m0 + trow;
+        const int mb = m < p.M ? m / p.tokens : 0;
+        const int mt = m < p.M ? m - mb * p.tokens : 0;
+        const float* pe_row = p.pe + mb * p.pe_bs + static_cast<int64_t>(mt) * 128;
+        for (int hh = 0; hh < 2; ++hh) {
+          const int head = (n0 - which * hidden) / 128 + hh;
+          const uint32_t tcol = tmem_base + lane_off + ab * kGN + hh * 128;
+          float ss = 0.f;
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tcol + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ss = fmaf(__uint_as_float(r[i]), __uint_as_float(r[i]), ss);
+          }
+          const float inv = 1.f / sqrtf(ss / 128.f + p.eps);
+          for (int half = 0; half < 2; ++half) {
+            uint32_t w[32];
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+              const int c = half * 2 + cc;
+              uint32_t r[32];
+              tmem_ld32(tcol + c * 32, r);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 16; i += 2) {
+                const int d = c * 32 + 2 * i;  // 2 RoPE pairs: d, d+1 and d+2, d+3
+                const float4 cs = m < p.M ? *reinterpret_cast<const float4*>(pe_row + d)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 wv = *reinterpret_cast<const float4*>(wn + d);
+                const float x0 = __uint_as_float(r[2 * i]) * inv * wv.x;
+                const float x1 = __uint_as_float(r[2 * i + 1]) * inv * wv.y;
+                const float x2 = __uint_as_float(r[2 * i + 2]) * inv * wv.z;
+                const float x3 = __uint_as_float(r[2 * i + 3]) * inv * wv.w;
+                w[cc * 16 + i] = gemm_pack_bf16x2(x0 * cs.x - x1 * cs.y, x0 * cs.y + x1 * cs.x);
+                w[cc * 16 + i + 1] = gemm_pack_bf16x2(x2 * cs.z - x3 * cs.w, x2 * cs.w + x3 * cs.z);
+              }
+            }
+            uint4* st4 = reinterpret_cast<uint4*>(stage_tile) + trow * 8;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              st4[j ^ (trow & 7)] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+            __syncwarp();
+#pragma unroll
+            for (int pass = 0; pass < 8; ++pass) {
+              const int rr = q * 32 + pass * 4 + (lane >> 3);
+              const int mm = m0 + rr;
+              const uint4 v = reinterpret_cast<const uint4*>(stage_tile)[rr * 8 + (sub ^ (rr & 7))];
+              if (mm < p.M) {
+                const int bb = mm / p.tokens, tt = mm - bb * p.tokens;
+                const int64_t row = (static_cast<int64_t>(bb) * p.heads + head) * p.tokens + tt;
+                *reinterpret_cast<uint4*>(dst_base + row * 128 + half * 64 + sub * 8) = v;
+              }
+            }
+            __syncwarp();
+          }
+        }
+      } else if (p.mode == B200_GEMM_RED_F32) {
         // f32 red-add: 32 columns per pass, 4 f32 (16 bytes) per lane.
         for (int c = 0; c < kGN / kEpiChunk; ++c) {
           const int col0 = n0 + c * kEpiChunk;
@@ -295,6 +372,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
               __nv_bfloat16* dst;
               if (p.mode == B200_GEMM_STORE_BF16) {
                 dst = static_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(m) * p.ldc + col;
+              } else if (p.mode == B200_GEMM_QKV) {  // V: token-major [B, T, H * 128]
+                dst = static_cast<__nv_bfloat16*>(p.v_out) + static_cast<int64_t>(m) * hidden +
+                      (col - 2 * hidden);
               } else {  // scatter: the owner's slot for this rank, over NVLink for others
                 const int owner = m / p.rows_per_owner;
                 const int64_t row = static_cast<int64_t>(p.src_slot) * p.rows_per_owner + (m - owner * p.rows_per_owner);
@@ -388,10 +468,22 @@ using namespace b200;
 namespace b200 {
 namespace {
 
+struct QkvArgs {
+  int32_t heads, tokens;
+  const float* pe;
+  int64_t pe_bs;
+  const float* norm_q;
+  const float* norm_k;
+  float eps;
+  void* q_out;
+  void* k_out;
+  void* v_out;
+};
+
 int launch_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
                 int32_t m, int32_t n, int32_t k, int32_t mode, int32_t* status,
                 cudaStream_t stream, void* const* peers, int32_t n_owners,
-                int32_t rows_per_owner, int32_t src_slot);
+                int32_t rows_per_owner, int32_t src_slot, const QkvArgs* qkv = nullptr);
 
 }  // namespace
 }  // namespace b200
@@ -402,6 +494,26 @@ extern "C" int b200_gemm(const void* a, int64_t lda, const void* b, int64_t ldb,
   if (mode != B200_GEMM_STORE_BF16 && mode != B200_GEMM_RED_F32) return B200_ERR_INVALID;
   return launch_gemm(a, lda, b, ldb, c, ldc, m, n, k, mode, status,
                      static_cast<cudaStream_t>(stream), nullptr, 0, 0, 0);
+}
+
+extern "C" int b200_qkv_norm_rope_gemm(const void* x, int64_t ldx, const void* w_qkv,
+                                       int32_t batch, int32_t tokens, int32_t heads,
+                                       int32_t in_features, const float* norm_q_w,
+                                       const float* norm_k_w, float eps, const float* pe,
+                                       int64_t pe_batch_stride, void* q_rot, void* k_rot,
+                                       void* v, int32_t* status, b200_stream_t stream) {
+  if (batch <= 0 || tokens <= 0 || heads <= 0 || heads % 2 != 0) return B200_ERR_INVALID;
+  if (!norm_q_w || !norm_k_w || !pe || !q_rot || !k_rot || !v) return B200_ERR_INVALID;
+  const void* ptrs[] = {norm_q_w, norm_k_w, pe, q_rot, k_rot, v};
+  for (const void* ptr : ptrs)
+    if (reinterpret_cast<uintptr_t>(ptr) & 15u) return B200_ERR_INVALID;
+  if (pe_batch_stride < 0 || pe_batch_stride % 4 != 0 || !(eps >= 0.f)) return B200_ERR_INVALID;
+  const int64_t m = static_cast<int64_t>(batch) * tokens;
+  if (m > 0x7fffffff) return B200_ERR_INVALID;
+  QkvArgs qa{heads, tokens, pe, pe_batch_stride, norm_q_w, norm_k_w, eps, q_rot, k_rot, v};
+  return launch_gemm(x, ldx, w_qkv, in_features, v, 3 * heads * 128, static_cast<int32_t>(m),
+                     3 * heads * 128, in_features, B200_GEMM_QKV, status,
+                     static_cast<cudaStream_t>(stream), nullptr, 0, 0, 0, &qa);
 }
 
 extern "C" int b200_gemm_scatter(const void* a, int64_t lda, const void* b, int64_t ldb,
@@ -424,7 +536,7 @@ namespace {
 int launch_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c, int64_t ldc,
                 int32_t m, int32_t n, int32_t k, int32_t mode, int32_t* status,
                 cudaStream_t stream, void* const* peers, int32_t n_owners,
-                int32_t rows_per_owner, int32_t src_slot) {
+                int32_t rows_per_owner, int32_t src_slot, const QkvArgs* qkv) {
   if (m < 0 || n < 0 || k < 0) return B200_ERR_INVALID;
   if (m == 0 || n == 0) return B200_OK;
   if (!a || !b || !c || !al16(a) || !al16(b) || !al16(c)) return B200_ERR_INVALID;
@@ -453,6 +565,21 @@ int launch_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c,
   for (int i = 0; i < n_owners; ++i) p.peers[i] = peers[i];
   p.rows_per_owner = rows_per_owner;
   p.src_slot = src_slot;
+  if (qkv) {
+    p.heads = qkv->heads;
+    p.tokens = qkv->tokens;
+    p.pe = qkv->pe;
+    p.pe_bs = qkv->pe_bs;
+    p.norm_q = qkv->norm_q;
+    p.norm_k = qkv->norm_k;
+    p.eps = qkv->eps;
+    p.q_out = qkv->q_out;
+    p.k_out = qkv->k_out;
+    p.v_out = qkv->v_out;
+  } else {
+    p.heads = 1;  // unused outside B200_GEMM_QKV
+    p.tokens = 1;
+  }
   const int grid = static_cast<int>(tiles < gemm_sms() ? tiles : gemm_sms());
   gemm_kernel<<<grid, kGThreads, kGSmemBytes, stream>>>(ma, mb, p);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;

@@ -88,3 +88,45 @@ def test_scatter_gather_emulated_ranks(cuda, world, T):
     for q in range(world):
         assert _rel(outs[q][:T].float(), want) < 5e-3
         assert torch.equal(outs[q], outs[0])   # identical on every rank
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,T,H,C", [(1, 256, 2, 256), (3, 200, 4, 512), (2, 4096, 32, 4096)])
+def test_qkv_norm_rope_gemm_matches_unfused(cuda, B, T, H, C):
+    """The fused Q/K/V projection (RMSNorm + RoPE in the epilogue) against the float32
+    reference of the same span, and the unfused path (bf16 GEMMs + b200_qk_norm_rope)."""
+    import numpy as np
+    from oracle import reference as ref
+    g = torch.Generator(device=cuda).manual_seed(B * T + H)
+    x = torch.randn(B * T, C, generator=g, device=cuda).bfloat16()
+    w = (torch.randn(3 * H * 128, C, generator=g, device=cuda) * C ** -0.5).bfloat16()
+    nq = 1 + 0.1 * torch.randn(128, generator=g, device=cuda)
+    nk = 1 + 0.1 * torch.randn(128, generator=g, device=cuda)
+    pes = []
+    for b in range(B):   # a different text length per batch row: different frame position
+        lay = ref.joint_layout(17 + 5 * b, None, [], (T // 8, 8) if T % 8 == 0 else (T, 1))
+        pes.append(ref.embed_nd(lay["img_shapes"], lay["image_pad_mask"])[17 + 5 * b:])
+    pe = torch.from_numpy(np.stack(pes)).to(cuda)
+    st = torch.zeros(1, dtype=torch.int32, device=cuda)
+    qr, kr, v = b200attn.qkv_norm_rope_gemm(x, w, B, T, H, nq, nk, pe, status=st)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    # float32 reference of to_q/to_k/to_v -> norm -> RoPE
+    y = (x.float() @ w.float().t()).view(B, T, 3, H, 128)
+    def norm_rope(t, wn):
+        t = t / torch.sqrt((t * t).mean(-1, keepdim=True) + 1e-6) * wn
+        c, s_ = pe[:, :, None, 0::2], pe[:, :, None, 1::2]
+        o = torch.empty_like(t)
+        o[..., 0::2] = t[..., 0::2] * c - t[..., 1::2] * s_
+        o[..., 1::2] = t[..., 0::2] * s_ + t[..., 1::2] * c
+        return o.transpose(1, 2)
+    want_q, want_k, want_v = norm_rope(y[:, :, 0], nq), norm_rope(y[:, :, 1], nk), y[:, :, 2]
+    assert _rel(qr.float(), want_q) < 5e-3 and _rel(kr.float(), want_k) < 5e-3
+    assert _rel(v.float(), want_v) < 5e-3
+    # the unfused path on the same inputs (bf16 rounding of the raw projections in between)
+    q0 = (x @ w[:H * 128].t()).view(B, T, H, 128)
+    k0 = (x @ w[H * 128:2 * H * 128].t()).view(B, T, H, 128)
+    for b in range(B):
+        uq, uk = b200attn.qk_norm_rope(q0[b:b + 1], k0[b:b + 1], nq, nk, 1e-6, pe[b])
+        assert _rel(qr[b:b + 1].float(), uq.float()) < 5e-3
+        assert _rel(kr[b:b + 1].float(), uk.float()) < 5e-3

@@ -230,3 +230,24 @@ def test_batch_rows_are_independent(tiny):
     alone = model.step(lat[1:], 0.3, one, model.target_pe(lengths[1:], GRID),
                        mmdit.cached_desc(one, 256, model.device)).cpu()
     assert rel(both[1:], alone) < 5e-3
+
+
+@pytest.mark.gpu
+def test_fused_qkv_step_matches_unfused(tiny):
+    """The cached step with the Q/K/V projections fused with norm + RoPE (one tcgen05 GEMM)
+    equals the unfused step (three GEMMs + b200_attn_fwd) up to bf16 rounding."""
+    w, _, R = tiny
+    lengths = [40, 72]
+    embs = _embs(lengths, 41)
+    g = torch.Generator().manual_seed(42)
+    lat = torch.randn(2, 256, 64, generator=g).to("cuda:0")
+    outs = []
+    for fused in (False, True):
+        model = mmdit.MMDiT(TINY, w, device="cuda:0", fused_qkv=fused)
+        cache = model.prefix_fill(embs)
+        outs.append(model.step(lat, 0.4, cache, model.target_pe(lengths, GRID),
+                               mmdit.cached_desc(cache, 256, model.device)).cpu())
+    assert rel(outs[1], outs[0]) < 1e-2
+    for b, n in enumerate(lengths):
+        want = R.forward_cached(lat[b].cpu(), 0.4, R.prefix_kv(embs[b].float(), GRID), n, GRID)
+        assert rel(outs[1][b], want) < 1.5e-2
