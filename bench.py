@@ -81,6 +81,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--weights", choices=["q4_k_m", "bf16"], default="q4_k_m",
                     help="config 5: block linears as GGUF Q4_K_M blocks (the config) or bf16")
+    ap.add_argument("--prompts", type=int, default=None,
+                    help="config 5: prompts in the batch (default 8; fewer only for profiling)")
     return ap.parse_args()
 
 
@@ -584,6 +586,8 @@ def run_denoise(args, cfg, rank, world, dev):
     gh, gw = cfg["grid"]
     T = gh * gw
     mcfg = mmdit.MMDiTConfig(layers=args.layers or cfg["layers"])
+    if args.prompts:
+        cfg = dict(cfg, prompts=args.prompts)
     pairs = c5_workload(cfg)
     mine = bdist.dp_assign(list(range(cfg["prompts"])), world, rank)
     lengths = [n for p in mine for n in pairs[p]]          # p0 pos, p0 neg, p1 pos, ...
