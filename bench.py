@@ -83,6 +83,10 @@ def parse_args():
                     help="config 5: block linears as GGUF Q4_K_M blocks (the config) or bf16")
     ap.add_argument("--prompts", type=int, default=None,
                     help="config 5: prompts in the batch (default 8; fewer only for profiling)")
+    ap.add_argument("--gemm", choices=["cublas", "b200"], default="cublas",
+                    help="config 5: the block linears' GEMM (cuBLAS or the tcgen05 kernel)")
+    ap.add_argument("--fused-qkv", action="store_true",
+                    help="config 5: Q/K/V projections with norm + RoPE in the GEMM epilogue")
     return ap.parse_args()
 
 
@@ -592,7 +596,8 @@ def run_denoise(args, cfg, rank, world, dev):
     mine = bdist.dp_assign(list(range(cfg["prompts"])), world, rank)
     lengths = [n for p in mine for n in pairs[p]]          # p0 pos, p0 neg, p1 pos, ...
     weights = mmdit.random_weights(mcfg, 2024, device=dev, std=0.02)   # same on every rank
-    model = mmdit.MMDiT(mcfg, weights, device=dev, weight_format=args.weights)
+    model = mmdit.MMDiT(mcfg, weights, device=dev, weight_format=args.weights,
+                        fused_qkv=args.fused_qkv, gemm=args.gemm)
     del weights
     torch.cuda.empty_cache()
     wbytes = model.weight_bytes()
@@ -692,6 +697,7 @@ def run_denoise(args, cfg, rank, world, dev):
                        "weights": (f"{args.weights}: block linears {wbytes / 1e9:.2f} GB "
                                    f"(7.1 B parameters)"),
                        "cfg_scale": cfg["cfg_scale"],
+                       "gemm": args.gemm + (" + fused QKV/norm/RoPE" if args.fused_qkv else ""),
                        "parallelism": f"dp{world} by prompt (pos/neg pairs together)",
                        "l2": "every step streams GBs of weights and activations (> L2)"},
             "step_tflops": (lin_f + attn_f) / (ms_step / 1e3) / 1e12,

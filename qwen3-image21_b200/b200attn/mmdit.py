@@ -174,7 +174,7 @@ class MMDiT:
     """The transformer on one GPU with bf16 weights (see module docstring)."""
 
     def __init__(self, cfg: MMDiTConfig, weights: dict, device="cuda", mlp_chunk_rows: int = 16384,
-                 weight_format: str = "bf16", fused_qkv: bool = False):
+                 weight_format: str = "bf16", fused_qkv: bool = False, gemm: str = "cublas"):
         """weight_format "bf16" keeps the block linears in bf16; "q4_k_m" stores them as GGUF
         Q4_K / Q6_K super-blocks (llama.cpp's Q4_K_M rule) and dequantises each block's six
         matrices to a bf16 scratch right before its GEMMs.  The other weights (img_in,
@@ -187,6 +187,9 @@ class MMDiT:
         import torch
         if weight_format not in ("bf16", "q4_k_m"):
             raise ValueError(f"unknown weight format {weight_format!r}")
+        if gemm not in ("cublas", "b200"):
+            raise ValueError(f"unknown GEMM {gemm!r}")
+        self.gemm_impl = gemm
         self.cfg, self.device = cfg, torch.device(device)
         self.mlp_chunk_rows = mlp_chunk_rows
         self.weight_format = weight_format
@@ -321,11 +324,16 @@ class MMDiT:
             out[p + "img_mlp.proj.weight"] = gp[f:].clone()
         return out
 
-    def _gemm(self, a, w, name):
-        """a [R, K] bf16 @ w[N, K]^T -> bf16 [R, N] (cuBLAS)."""
+    def _gemm(self, a, w, name, out=None):
+        """a [R, K] bf16 @ w[N, K]^T -> bf16 [R, N]: cuBLAS, or this package's tcgen05 GEMM
+        (gemm="b200")."""
         import torch
-        out = self._buf(name, (a.shape[0], w.shape[0]), torch.bfloat16)
-        torch.mm(a, w.t(), out=out)
+        if out is None:
+            out = self._buf(name, (a.shape[0], w.shape[0]), torch.bfloat16)
+        if self.gemm_impl == "b200":
+            b200attn.gemm(a, w, out=out)
+        else:
+            torch.mm(a, w.t(), out=out)
         return out
 
     # -- the block loop -----------------------------------------------------------
@@ -382,7 +390,7 @@ class MMDiT:
                 r1 = min(R, r0 + self.mlp_chunk_rows)
                 gp = self._gemm(y[r0:r1], blk["wgp"], "gp")
                 hh = b200attn.swiglu(gp, self._buf("h", (r1 - r0, cfg.ffn), torch.bfloat16))
-                torch.mm(hh, blk["wmo"].t(), out=mo[r0:r1])
+                self._gemm(hh, blk["wmo"], "mo", out=mo[r0:r1])
             last = i + 1 == len(self.blocks)
             if not last:
                 b200attn.residual_adaln(x, mo, gate2, scale1, y, rows_per_mod=R)  # next norm1

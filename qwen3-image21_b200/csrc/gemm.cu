@@ -26,6 +26,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <mutex>
 
 #include "../../include/b200_attn.h"
@@ -52,10 +53,10 @@ constexpr uint32_t kGTmemCols = 512;                         // 2 accumulators x
 
 constexpr int kMaxOwners = 8;
 
-constexpr int kGroupM = 8;  // row blocks per raster group
-
 struct GemmParams {
   int32_t M, N, K;
+  int32_t tile_m;      // rows per output tile: 128 (one CTA) or 256 (a CTA pair)
+  int32_t group_m;     // row blocks per raster group (see tile_coords)
   int32_t tiles_m, tiles_n, tiles;
   int32_t mode;        // B200_GEMM_STORE_BF16 / _RED_F32 / _SCATTER_BF16
   int64_t ldc;         // elements between rows of C
@@ -99,22 +100,171 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
 }
 
 
-// Grouped raster: tiles run in groups of kGroupM row blocks, row-block-fastest inside a
-// group, so the CTAs in flight share a few A row blocks and a band of B column blocks
-// (both stay in L2 even when B is larger than L2).
+// Grouped raster: tiles run in groups of group_m row blocks, row-block-fastest inside a
+// group.  The group's A rows (sized on the host to about half of L2) stay in L2 while the
+// group walks every column block, and the tiles in flight share a narrow band of B: A
+// comes from HBM about once and B once per group, also when B is larger than L2.
 __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& m0, int& n0) {
-  const int per_group = kGroupM * p.tiles_n;
+  const int per_group = p.group_m * p.tiles_n;
   const int g = t / per_group;
-  const int first = g * kGroupM;
-  const int gm = min(kGroupM, p.tiles_m - first);
+  const int first = g * p.group_m;
+  const int gm = min(p.group_m, p.tiles_m - first);
   const int local = t - g * per_group;
-  m0 = (first + local % gm) * kGM;
+  m0 = (first + local % gm) * p.tile_m;
   n0 = (local / gm) * kGN;
 }
 
 __device__ __forceinline__ void gemm_error(const GemmParams& p, volatile int* abort_flag, int code) {
   *abort_flag = 1;
   if (p.status) atomicCAS(p.status, 0, code);
+}
+
+// One tile's epilogue by the 128 epilogue threads of a CTA: accumulator `ab` of TMEM
+// (this thread's lane quadrant `q`, row `trow` of the tile), output rows m0 + trow.
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tmem_base,
+                                              uint32_t lane_off, int ab, int m0, int n0,
+                                              int q, int lane, int trow, float* stage_tile) {
+  // staging tile: row r holds 32 f32 = 8 chunks of 16 bytes, chunk j at (j ^ (r & 7))
+  float4* st_row = reinterpret_cast<float4*>(stage_tile) + trow * 8;
+  const int sub = lane & 7;  // 16-byte chunk this lane moves in a pass
+  const int hidden = p.heads * 128;
+  const int which = p.mode == B200_GEMM_QKV ? n0 / hidden : -1;
+  if (which == 0 || which == 1) {
+    // Q or K of two heads: RMSNorm over each head's 128 values (a first pass over TMEM
+    // for the sum of squares), then RoPE, bf16, head-major rows, 64 columns per pass.
+    const float* wn = which == 0 ? p.norm_q : p.norm_k;
+    __nv_bfloat16* dst_base = static_cast<__nv_bfloat16*>(which == 0 ? p.q_out : p.k_out);
+    const int m = m0 + trow;
+    const int mb = m < p.M ? m / p.tokens : 0;
+    const int mt = m < p.M ? m - mb * p.tokens : 0;
+    const float* pe_row = p.pe + mb * p.pe_bs + static_cast<int64_t>(mt) * 128;
+    for (int hh = 0; hh < 2; ++hh) {
+      const int head = (n0 - which * hidden) / 128 + hh;
+      const uint32_t tcol = tmem_base + lane_off + ab * kGN + hh * 128;
+      float ss = 0.f;
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tcol + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ss = fmaf(__uint_as_float(r[i]), __uint_as_float(r[i]), ss);
+      }
+      const float inv = 1.f / sqrtf(ss / 128.f + p.eps);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t w[32];
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = half * 2 + cc;
+          uint32_t r[32];
+          tmem_ld32(tcol + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const int d = c * 32 + 2 * i;  // 2 RoPE pairs: d, d+1 and d+2, d+3
+            const float4 cs = m < p.M ? *reinterpret_cast<const float4*>(pe_row + d)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 wv = *reinterpret_cast<const float4*>(wn + d);
+            const float x0 = __uint_as_float(r[2 * i]) * inv * wv.x;
+            const float x1 = __uint_as_float(r[2 * i + 1]) * inv * wv.y;
+            const float x2 = __uint_as_float(r[2 * i + 2]) * inv * wv.z;
+            const float x3 = __uint_as_float(r[2 * i + 3]) * inv * wv.w;
+            w[cc * 16 + i] = gemm_pack_bf16x2(x0 * cs.x - x1 * cs.y, x0 * cs.y + x1 * cs.x);
+            w[cc * 16 + i + 1] = gemm_pack_bf16x2(x2 * cs.z - x3 * cs.w, x2 * cs.w + x3 * cs.z);
+          }
+        }
+        uint4* st4 = reinterpret_cast<uint4*>(stage_tile) + trow * 8;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          st4[j ^ (trow & 7)] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int pass = 0; pass < 8; ++pass) {
+          const int rr = q * 32 + pass * 4 + (lane >> 3);
+          const int mm = m0 + rr;
+          const uint4 v = reinterpret_cast<const uint4*>(stage_tile)[rr * 8 + (sub ^ (rr & 7))];
+          if (mm < p.M) {
+            const int bb = mm / p.tokens, tt = mm - bb * p.tokens;
+            const int64_t row = (static_cast<int64_t>(bb) * p.heads + head) * p.tokens + tt;
+            *reinterpret_cast<uint4*>(dst_base + row * 128 + half * 64 + sub * 8) = v;
+          }
+        }
+        __syncwarp();
+      }
+    }
+  } else if (p.mode == B200_GEMM_RED_F32) {
+    // f32 red-add: 32 columns per pass, 4 f32 (16 bytes) per lane.
+    for (int c = 0; c < kGN / kEpiChunk; ++c) {
+      const int col0 = n0 + c * kEpiChunk;
+      if (col0 >= p.N) break;  // same for every thread of the tile
+      uint32_t r[32];
+      tmem_ld32(tmem_base + lane_off + ab * kGN + c * kEpiChunk, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        st_row[j ^ (trow & 7)] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                             __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+      __syncwarp();
+      // This warp's 32 rows, 4 per pass: lane -> row (lane / 8), chunk (lane % 8).
+#pragma unroll
+      for (int pass = 0; pass < 8; ++pass) {
+        const int rr = q * 32 + pass * 4 + (lane >> 3);
+        const int m = m0 + rr;
+        const float4 v =
+            reinterpret_cast<const float4*>(stage_tile)[rr * 8 + (sub ^ (rr & 7))];
+        if (m < p.M)
+          red_add_v4(static_cast<float*>(p.C) + static_cast<int64_t>(m) * p.ldc + col0 + sub * 4,
+                     v.x, v.y, v.z, v.w);
+      }
+      __syncwarp();
+    }
+  } else {
+    // bf16 store / scatter: 64 columns per pass (two TMEM loads), 8 bf16 (16 bytes) per
+    // lane, so each row leaves as one 128-byte segment.
+    for (int c = 0; c < kGN / 64; ++c) {
+      const int col0 = n0 + c * 64;
+      if (col0 >= p.N) break;  // same for every thread of the tile
+      const bool two = col0 + 32 < p.N;
+      uint32_t r[32], w[32];
+      tmem_ld32(tmem_base + lane_off + ab * kGN + c * 64, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = gemm_pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+      if (two) {
+        tmem_ld32(tmem_base + lane_off + ab * kGN + c * 64 + 32, r);
+        tmem_wait_ld();
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        w[16 + i] = two ? gemm_pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])) : 0u;
+      uint4* st4 = reinterpret_cast<uint4*>(stage_tile) + trow * 8;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        st4[j ^ (trow & 7)] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+      __syncwarp();
+#pragma unroll
+      for (int pass = 0; pass < 8; ++pass) {
+        const int rr = q * 32 + pass * 4 + (lane >> 3);
+        const int m = m0 + rr;
+        const uint4 v = reinterpret_cast<const uint4*>(stage_tile)[rr * 8 + (sub ^ (rr & 7))];
+        const int col = col0 + sub * 8;
+        if (m < p.M && col < p.N) {
+          __nv_bfloat16* dst;
+          if (p.mode == B200_GEMM_STORE_BF16) {
+            dst = static_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(m) * p.ldc + col;
+          } else if (p.mode == B200_GEMM_QKV) {  // V: token-major [B, T, H * 128]
+            dst = static_cast<__nv_bfloat16*>(p.v_out) + static_cast<int64_t>(m) * hidden +
+                  (col - 2 * hidden);
+          } else {  // scatter: the owner's slot for this rank, over NVLink for others
+            const int owner = m / p.rows_per_owner;
+            const int64_t row = static_cast<int64_t>(p.src_slot) * p.rows_per_owner + (m - owner * p.rows_per_owner);
+            dst = static_cast<__nv_bfloat16*>(p.peers[owner]) + row * p.ldc + col;
+          }
+          *reinterpret_cast<uint4*>(dst) = v;
+        }
+      }
+      __syncwarp();
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kGThreads, 1)
@@ -233,9 +383,6 @@ __global__ void __launch_bounds__(kGThreads, 1)
     const int q = warp & 3;                 // TMEM lane quadrant of this warp
     const int trow = q * 32 + lane;         // this thread's row of the tile
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    // staging tile: row r holds 32 f32 = 8 chunks of 16 bytes, chunk j at (j ^ (r & 7))
-    float4* st_row = reinterpret_cast<float4*>(stage_tile) + trow * 8;
-    const int sub = lane & 7;               // 16-byte chunk this lane moves in a pass
     int lt = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++lt) {
@@ -248,144 +395,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
       tc_fence_after();
       int m0, n0;
       tile_coords(p, tile, m0, n0);
-      const int hidden = p.heads * 128;
-      const int which = p.mode == B200_GEMM_QKV ? n0 / hidden : -1;
-      if (which == 0 || which == 1) {
-        // Q or K of two heads: RMSNorm over each head's 128 values (a first pass over TMEM
-        // for the sum of squares), then RoPE, bf16, head-major rows, 64 columns per pass.
-        const float* wn = which == 0 ? p.norm_q : p.norm_k;
-        __nv_bfloat16* dst_base = static_cast<__nv_bfloat16*>(which == 0 ? p.q_out : p.k_out);
-        const int m = m0 + trow;
-        const int mb = m < p.M ? m / p.tokens : 0;
-        const int mt = m < p.M ? m - mb * p.tokens : 0;
-        const float* pe_row = p.pe + mb * p.pe_bs + static_cast<int64_t>(mt) * 128;
-        for (int hh = 0; hh < 2; ++hh) {
-          const int head = (n0 - which * hidden) / 128 + hh;
-          const uint32_t tcol = tmem_base + lane_off + ab * kGN + hh * 128;
-          float ss = 0.f;
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tcol + c * 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) ss = fmaf(__uint_as_float(r[i]), __uint_as_float(r[i]), ss);
-          }
-          const float inv = 1.f / sqrtf(ss / 128.f + p.eps);
-          for (int half = 0; half < 2; ++half) {
-            uint32_t w[32];
-#pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-              const int c = half * 2 + cc;
-              uint32_t r[32];
-              tmem_ld32(tcol + c * 32, r);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 16; i += 2) {
-                const int d = c * 32 + 2 * i;  // 2 RoPE pairs: d, d+1 and d+2, d+3
-                const float4 cs = m < p.M ? *reinterpret_cast<const float4*>(pe_row + d)
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-                const float4 wv = *reinterpret_cast<const float4*>(wn + d);
-                const float x0 = __uint_as_float(r[2 * i]) * inv * wv.x;
-                const float x1 = __uint_as_float(r[2 * i + 1]) * inv * wv.y;
-                const float x2 = __uint_as_float(r[2 * i + 2]) * inv * wv.z;
-                const float x3 = __uint_as_float(r[2 * i + 3]) * inv * wv.w;
-                w[cc * 16 + i] = gemm_pack_bf16x2(x0 * cs.x - x1 * cs.y, x0 * cs.y + x1 * cs.x);
-                w[cc * 16 + i + 1] = gemm_pack_bf16x2(x2 * cs.z - x3 * cs.w, x2 * cs.w + x3 * cs.z);
-              }
-            }
-            uint4* st4 = reinterpret_cast<uint4*>(stage_tile) + trow * 8;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              st4[j ^ (trow & 7)] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-            __syncwarp();
-#pragma unroll
-            for (int pass = 0; pass < 8; ++pass) {
-              const int rr = q * 32 + pass * 4 + (lane >> 3);
-              const int mm = m0 + rr;
-              const uint4 v = reinterpret_cast<const uint4*>(stage_tile)[rr * 8 + (sub ^ (rr & 7))];
-              if (mm < p.M) {
-                const int bb = mm / p.tokens, tt = mm - bb * p.tokens;
-                const int64_t row = (static_cast<int64_t>(bb) * p.heads + head) * p.tokens + tt;
-                *reinterpret_cast<uint4*>(dst_base + row * 128 + half * 64 + sub * 8) = v;
-              }
-            }
-            __syncwarp();
-          }
-        }
-      } else if (p.mode == B200_GEMM_RED_F32) {
-        // f32 red-add: 32 columns per pass, 4 f32 (16 bytes) per lane.
-        for (int c = 0; c < kGN / kEpiChunk; ++c) {
-          const int col0 = n0 + c * kEpiChunk;
-          if (col0 >= p.N) break;  // same for every thread of the tile
-          uint32_t r[32];
-          tmem_ld32(tmem_base + lane_off + ab * kGN + c * kEpiChunk, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            st_row[j ^ (trow & 7)] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-          __syncwarp();
-          // This warp's 32 rows, 4 per pass: lane -> row (lane / 8), chunk (lane % 8).
-#pragma unroll
-          for (int pass = 0; pass < 8; ++pass) {
-            const int rr = q * 32 + pass * 4 + (lane >> 3);
-            const int m = m0 + rr;
-            const float4 v =
-                reinterpret_cast<const float4*>(stage_tile)[rr * 8 + (sub ^ (rr & 7))];
-            if (m < p.M)
-              red_add_v4(static_cast<float*>(p.C) + static_cast<int64_t>(m) * p.ldc + col0 + sub * 4,
-                         v.x, v.y, v.z, v.w);
-          }
-          __syncwarp();
-        }
-      } else {
-        // bf16 store / scatter: 64 columns per pass (two TMEM loads), 8 bf16 (16 bytes) per
-        // lane, so each row leaves as one 128-byte segment.
-        for (int c = 0; c < kGN / 64; ++c) {
-          const int col0 = n0 + c * 64;
-          if (col0 >= p.N) break;  // same for every thread of the tile
-          const bool two = col0 + 32 < p.N;
-          uint32_t r[32], w[32];
-          tmem_ld32(tmem_base + lane_off + ab * kGN + c * 64, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) w[i] = gemm_pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-          if (two) {
-            tmem_ld32(tmem_base + lane_off + ab * kGN + c * 64 + 32, r);
-            tmem_wait_ld();
-          }
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            w[16 + i] = two ? gemm_pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])) : 0u;
-          uint4* st4 = reinterpret_cast<uint4*>(stage_tile) + trow * 8;
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            st4[j ^ (trow & 7)] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-          __syncwarp();
-#pragma unroll
-          for (int pass = 0; pass < 8; ++pass) {
-            const int rr = q * 32 + pass * 4 + (lane >> 3);
-            const int m = m0 + rr;
-            const uint4 v = reinterpret_cast<const uint4*>(stage_tile)[rr * 8 + (sub ^ (rr & 7))];
-            const int col = col0 + sub * 8;
-            if (m < p.M && col < p.N) {
-              __nv_bfloat16* dst;
-              if (p.mode == B200_GEMM_STORE_BF16) {
-                dst = static_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(m) * p.ldc + col;
-              } else if (p.mode == B200_GEMM_QKV) {  // V: token-major [B, T, H * 128]
-                dst = static_cast<__nv_bfloat16*>(p.v_out) + static_cast<int64_t>(m) * hidden +
-                      (col - 2 * hidden);
-              } else {  // scatter: the owner's slot for this rank, over NVLink for others
-                const int owner = m / p.rows_per_owner;
-                const int64_t row = static_cast<int64_t>(p.src_slot) * p.rows_per_owner + (m - owner * p.rows_per_owner);
-                dst = static_cast<__nv_bfloat16*>(p.peers[owner]) + row * p.ldc + col;
-              }
-              *reinterpret_cast<uint4*>(dst) = v;
-            }
-          }
-          __syncwarp();
-        }
-      }
+      epilogue_tile(p, tmem_base, lane_off, ab, m0, n0, q, lane, trow, stage_tile);
       tc_fence_before();
       mbar_arrive(acc_empty + ab);
     }
@@ -400,6 +410,248 @@ __global__ void __launch_bounds__(kGThreads, 1)
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kGTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ CTA-pair variant
+// Two CTAs of a cluster compute one 256 x 256 tile with tcgen05.mma.cta_group::2: each CTA
+// loads its 128 rows of A and its 128 rows of B (the pair shares B through the tensor
+// cores), so a CTA moves 32 KiB per 64-deep K step instead of 48 KiB, and the ring holds 6
+// steps.  CTA 0 issues the MMAs; both CTAs' TMA bytes land on CTA 0's `full` barriers;
+// commits reach both CTAs' barriers; each CTA's epilogue reads its own 128 rows of the
+// accumulator from its TMEM and arrives once on CTA 0's `acc_empty`.
+constexpr int kG2Stages = 6;
+constexpr int kHalfTileBytes = 128 * kGK * 2;                // 16 KiB: 128 rows x 64
+constexpr int kStage2Bytes = 2 * kHalfTileBytes;             // A half + B half
+constexpr int kStage2Smem = kG2Stages * kStage2Bytes;        // 192 KiB
+constexpr int kG2BarOff = kStage2Smem + kEpiSmem;
+constexpr int kG2SmemBytes = kG2BarOff + 256 + 1024;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of both CTAs; release / acquire orders shared-memory writes across the pair.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion bytes count on the
+// leader CTA's barrier at the same offset (the peer bit of the address cleared).  No
+// multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                                 int32_t c0, int32_t c1) {
+  const uint32_t mbar = smem_addr(bar) & 0xFEFFFFFFu;
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(mbar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+template <uint32_t kOffA, uint32_t kOffB>
+__device__ __forceinline__ void mma_pair_ss_off(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi,
+                                                uint32_t b_lo, uint32_t b_hi, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 la, lb;\n\t.reg .b64 da, db;\n\t"
+      "add.u32 la, %1, %7;\n\tadd.u32 lb, %3, %8;\n\t"
+      "mov.b64 da, {la, %2};\n\tmov.b64 db, {lb, %4};\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate), "n"(kOffA),
+      "n"(kOffB)
+      : "memory");
+}
+
+// Arrive once on the barrier at this offset in both CTAs of the pair when every tcgen05
+// operation issued so far is done.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_addr(bar)),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+// Arrive on the barrier at this offset in CTA `cta` of the cluster.
+__device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, uint32_t cta) {
+  asm volatile(
+      "{\n\t.reg .b32 ra;\n\tmapa.shared::cluster.u32 ra, %0, %1;\n\t"
+      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_addr(bar)),
+      "r"(cta)
+      : "memory");
+}
+
+__device__ __forceinline__ void epilogue_barrier() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a,
+                     const __grid_constant__ CUtensorMap tm_b, const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* stage_tile = reinterpret_cast<float*>(smem + kStage2Smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kG2BarOff);
+  uint64_t* full = bars;                      // [kG2Stages], used in CTA 0
+  uint64_t* empty = bars + kG2Stages;         // [kG2Stages]
+  uint64_t* acc_full = bars + 2 * kG2Stages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;         // [2], used in CTA 0
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(acc_empty + 3);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int nk = (p.K + kGK - 1) / kGK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kG2Stages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 2);  // one arrival per CTA of the pair
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_slot, kGTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers and TMEM are ready before any cross-CTA traffic
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_a);
+      tma_prefetch_desc(&tm_b);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.tiles && ok; tile += npairs) {
+        int m0, n0;
+        tile_coords(p, tile, m0, n0);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kG2Stages;
+          const uint32_t ph = (it / kG2Stages) & 1;
+          if (!mbar_wait(empty + s, ph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * kStage2Bytes;
+          if (rank == 0) mbar_expect_tx(full + s, 2 * kStage2Bytes);
+          tma_load_2d_pair(sa, &tm_a, full + s, kb * kGK, m0 + static_cast<int>(rank) * 128);
+          tma_load_2d_pair(sa + kHalfTileBytes, &tm_b, full + s, kb * kGK,
+                           n0 + static_cast<int>(rank) * 128);
+        }
+      }
+      if (!ok) {
+        gemm_error(p, abort_flag, 1);
+        if (rank == 0)  // let issued copies land before shared memory is released
+          for (int s = 0; s < kG2Stages; ++s) mbar_wait(full + s, 0);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (CTA 0)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(2 * kGM, kGN, 0, 0);
+      const uint64_t d0 = smem_desc(smem_addr(smem), 16, 1024);
+      const uint32_t hi = static_cast<uint32_t>(d0 >> 32);
+      const uint32_t lo0 = static_cast<uint32_t>(d0);
+      uint32_t it = 0;
+      int lt = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.tiles && ok; tile += npairs, ++lt) {
+        const int ab = lt & 1;
+        const uint32_t aph = (lt >> 1) & 1;
+        if (!mbar_wait(acc_empty + ab, aph ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + ab * kGN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kG2Stages;
+          const uint32_t ph = (it / kG2Stages) & 1;
+          if (!mbar_wait(full + s, ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = lo0 + ((s * kStage2Bytes) >> 4);
+          const uint32_t b = a + (kHalfTileBytes >> 4);
+          mma_pair_ss_off<0, 0>(d, a, hi, b, hi, idesc, kb > 0 ? 1u : 0u);
+          mma_pair_ss_off<2, 2>(d, a, hi, b, hi, idesc, 1u);
+          mma_pair_ss_off<4, 4>(d, a, hi, b, hi, idesc, 1u);
+          mma_pair_ss_off<6, 6>(d, a, hi, b, hi, idesc, 1u);
+          mma_commit_pair(empty + s);
+        }
+        if (!ok) break;
+        mma_commit_pair(acc_full + ab);
+      }
+      if (!ok) gemm_error(p, abort_flag, 2);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int trow = q * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    int lt = 0;
+    bool ok = true;
+    for (int tile = pair; tile < p.tiles; tile += npairs, ++lt) {
+      const int ab = lt & 1;
+      const uint32_t aph = (lt >> 1) & 1;
+      if (!mbar_wait(acc_full + ab, aph, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      int m0, n0;
+      tile_coords(p, tile, m0, n0);
+      epilogue_tile(p, tmem_base, lane_off, ab, m0 + static_cast<int>(rank) * 128, n0, q, lane,
+                    trow, stage_tile);
+      tc_fence_before();
+      epilogue_barrier();  // all 128 rows of this CTA read
+      if (threadIdx.x == 4 * 32) {
+        if (rank == 0) mbar_arrive(acc_empty + ab);
+        else mbar_arrive_remote(acc_empty + ab, 0);
+      }
+    }
+    if (!ok) gemm_error(p, abort_flag, 3);
+    if (p.mode != B200_GEMM_STORE_BF16) __threadfence_system();
+  }
+
+  tc_fence_before();
+  cluster_sync();  // neither CTA leaves while the other may still signal its barriers
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kGTmemCols);
   }
 }
 
@@ -452,13 +704,26 @@ int ensure_gemm_attrs() {
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
   if (major != 10 || minor != 0) return B200_ERR_UNSUPPORTED;
   if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kGSmemBytes) != cudaSuccess)
+                           kGSmemBytes) != cudaSuccess ||
+      cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kG2SmemBytes) != cudaSuccess)
     return B200_ERR_CUDA;
   done_dev = dev;
   return B200_OK;
 }
 
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// CTA-pair (256-row) tiles from 512 rows up; B200_GEMM_PAIR=0 / 1 forces one-CTA / pair
+// tiles (for comparisons).
+bool use_pair_tiles(int32_t m) {
+  static const int forced = [] {
+    const char* e = std::getenv("B200_GEMM_PAIR");
+    return e ? (e[0] == '1' ? 1 : 0) : -1;
+  }();
+  if (forced >= 0) return forced == 1;
+  return m >= 512;
+}
 
 }  // namespace
 }  // namespace b200
@@ -546,15 +811,22 @@ int launch_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c,
   if (n % 32 != 0 || ldc < n || ldc % 8 != 0) return B200_ERR_INVALID;
   int rc = ensure_gemm_attrs();
   if (rc != B200_OK) return rc;
+  const bool pair = use_pair_tiles(m);
   CUtensorMap ma{}, mb{};
   if ((rc = make_map_2d(&ma, a, m, k, lda, kGM)) != B200_OK) return rc;
-  if ((rc = make_map_2d(&mb, b, n, k, ldb, kGN)) != B200_OK) return rc;
+  if ((rc = make_map_2d(&mb, b, n, k, ldb, pair ? kGN / 2 : kGN)) != B200_OK) return rc;
   GemmParams p{};
   p.M = m;
   p.N = n;
   p.K = k;
+  p.tile_m = pair ? 2 * kGM : kGM;
   p.tiles_n = (n + kGN - 1) / kGN;
-  p.tiles_m = (m + kGM - 1) / kGM;
+  p.tiles_m = (m + p.tile_m - 1) / p.tile_m;
+  {  // A rows of one raster group: about 64 MiB (half of L2)
+    const int64_t rows_bytes = static_cast<int64_t>(p.tile_m) * k * 2;
+    const int64_t g = (int64_t{64} << 20) / rows_bytes;
+    p.group_m = static_cast<int32_t>(g < 1 ? 1 : (g > p.tiles_m ? p.tiles_m : g));
+  }
   const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
   if (tiles > 0x7fffffff) return B200_ERR_INVALID;
   p.tiles = static_cast<int32_t>(tiles);
@@ -580,8 +852,14 @@ int launch_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, void* c,
     p.heads = 1;  // unused outside B200_GEMM_QKV
     p.tokens = 1;
   }
-  const int grid = static_cast<int>(tiles < gemm_sms() ? tiles : gemm_sms());
-  gemm_kernel<<<grid, kGThreads, kGSmemBytes, stream>>>(ma, mb, p);
+  if (pair) {
+    const int pairs = gemm_sms() / 2;
+    const int grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
+    gemm_pair_kernel<<<grid, kGThreads, kG2SmemBytes, stream>>>(ma, mb, p);
+  } else {
+    const int grid = static_cast<int>(tiles < gemm_sms() ? tiles : gemm_sms());
+    gemm_kernel<<<grid, kGThreads, kGSmemBytes, stream>>>(ma, mb, p);
+  }
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 

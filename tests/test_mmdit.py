@@ -251,3 +251,21 @@ def test_fused_qkv_step_matches_unfused(tiny):
     for b, n in enumerate(lengths):
         want = R.forward_cached(lat[b].cpu(), 0.4, R.prefix_kv(embs[b].float(), GRID), n, GRID)
         assert rel(outs[1][b], want) < 1.5e-2
+
+
+@pytest.mark.gpu
+def test_tcgen05_gemm_model_matches_cublas_model(tiny):
+    """The model with its block linears on the tcgen05 GEMM equals the cuBLAS model up to
+    bf16 rounding of the GEMM outputs."""
+    w, _, _ = tiny
+    lengths = [40, 72]
+    embs = _embs(lengths, 51)
+    g = torch.Generator().manual_seed(52)
+    lat = torch.randn(2, 256, 64, generator=g).to("cuda:0")
+    outs = []
+    for impl in ("cublas", "b200"):
+        model = mmdit.MMDiT(TINY, w, device="cuda:0", gemm=impl, mlp_chunk_rows=300)
+        cache = model.prefix_fill(embs)
+        outs.append(model.step(lat, 0.6, cache, model.target_pe(lengths, GRID),
+                               mmdit.cached_desc(cache, 256, model.device)).cpu())
+    assert rel(outs[1], outs[0]) < 1e-2
