@@ -663,17 +663,20 @@ __global__ void __launch_bounds__(64) wait_selftest_kernel(int32_t* status, uint
 }
 
 // ------------------------------------------------------------------ norm + RoPE
-// A group of 16 lanes handles kNormRows consecutive (b, t, h) rows of 128 values; lane i
-// of the group owns elements 8i..8i+7 (RoPE pairs 4i..4i+3) and all loads of the group's
-// rows are issued before any arithmetic.  y = RoPE(x / sqrt(mean(x^2) + eps) * w) in f32,
-// rounded to bf16 once; y is written head-major.
+// One warp per token (b, t) at a time (grid-stride over the B*T tokens); a group of 4
+// lanes owns one head's row of 128 values, 8 heads side by side, two rows in flight per
+// lane.  Lane `sub` of a group holds the 8-value chunks j*4 + sub (j = 0..3), so each load
+// or store instruction covers 64 contiguous bytes per row.  The token's RoPE table row
+// and the norm weights are loaded once and reused for every head.  Per row:
+// y = RoPE(x / sqrt(mean(x^2) + eps) * w) in f32, rounded to bf16 once, written
+// head-major; the sum of squares is 2 shuffles over the group.
 struct NormRopeJob {
   const __nv_bfloat16* x;
   __nv_bfloat16* y;
   const float* w;  // NULL: no norm
 };
 
-constexpr int kNormRows = 4;
+constexpr int kNrRows = 2;  // rows (heads) in flight per lane
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -684,7 +687,14 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   }
 }
 
-__global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeJob j0, NormRopeJob j1,
+__device__ __forceinline__ void load_f32x8(const float* p, float (&f)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+__global__ void __launch_bounds__(256, 2) norm_rope_kernel(NormRopeJob j0, NormRopeJob j1,
                                                          NormRopeJob j2, int B, int T, int H,
                                                          float eps, const float* pe,
                                                          int64_t pe_bs, int rope_mask,
@@ -693,71 +703,84 @@ __global__ void __launch_bounds__(256) norm_rope_kernel(NormRopeJob j0, NormRope
   // a separate memset before the attention launch that follows on the same stream.
   if (zero && blockIdx.x == 0 && blockIdx.y == 0 && static_cast<int>(threadIdx.x) < n_zero)
     zero[threadIdx.x] = 0;
-  // Host guarantees B * T * H < 2^31, so row indices fit 32 bits.
   const NormRopeJob job = blockIdx.y == 0 ? j0 : (blockIdx.y == 1 ? j1 : j2);
   const bool rope = pe != nullptr && ((rope_mask >> blockIdx.y) & 1);
+  const bool norm = job.w != nullptr;
   const int lane = threadIdx.x & 31;
-  const int sub = lane & 15;
-  const unsigned half_mask = lane < 16 ? 0x0000ffffu : 0xffff0000u;
-  const uint32_t group = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
-  const uint32_t rows = static_cast<uint32_t>(B) * T * H;
-  const uint32_t r0 = group * kNormRows;
-  if (r0 >= rows) return;  // the whole 16-lane group leaves together
-  uint4 xv[kNormRows];
+  const int sub = lane & 3;   // chunk column within the group
+  const int hl = lane >> 2;   // head offset within the warp's 8
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  float w[4][8];
+  if (norm) {
 #pragma unroll
-  for (int i = 0; i < kNormRows; ++i)
-    xv[i] = r0 + i < rows ? *reinterpret_cast<const uint4*>(job.x + static_cast<size_t>(r0 + i) * kD + sub * 8)
-                          : make_uint4(0, 0, 0, 0);
-  float w[8];
-  if (job.w) {
-    const float4 wa = *reinterpret_cast<const float4*>(job.w + sub * 8);
-    const float4 wb = *reinterpret_cast<const float4*>(job.w + sub * 8 + 4);
-    w[0] = wa.x; w[1] = wa.y; w[2] = wa.z; w[3] = wa.w;
-    w[4] = wb.x; w[5] = wb.y; w[6] = wb.z; w[7] = wb.w;
+    for (int j = 0; j < 4; ++j) load_f32x8(job.w + j * 32 + sub * 8, w[j]);
   }
-  // (b, t, h) of row r0; later rows step h, then t, then b.
-  uint32_t h = r0 % H, bt = r0 / H;
-  uint32_t t = bt % T, b = bt / T;
+  const int64_t tokens = static_cast<int64_t>(B) * T;
+  for (int64_t tok = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       tok < tokens; tok += warps) {
+    const int b = static_cast<int>(tok / T), t = static_cast<int>(tok - static_cast<int64_t>(b) * T);
+    float cs[4][8];
+    if (rope) {
+      const float* pr = pe + static_cast<int64_t>(b) * pe_bs + static_cast<int64_t>(t) * kD;
 #pragma unroll
-  for (int i = 0; i < kNormRows; ++i) {
-    const uint32_t row = r0 + i;
-    float v[8];
-    bf16x8_to_f32(xv[i], v);
-    if (job.w) {
-      float ss = 0.f;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(half_mask, ss, o);
-      const float inv = 1.f / sqrtf(ss / static_cast<float>(kD) + eps);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = v[e] * inv * w[e];
+      for (int j = 0; j < 4; ++j) load_f32x8(pr + j * 32 + sub * 8, cs[j]);
     }
-    if (row < rows) {
-      if (rope) {
-        const float* pr = pe + static_cast<int64_t>(b) * pe_bs + static_cast<size_t>(t) * kD + sub * 8;
-        const float4 ca = *reinterpret_cast<const float4*>(pr);
-        const float4 cb = *reinterpret_cast<const float4*>(pr + 4);
-        const float cs[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+    const __nv_bfloat16* xt = job.x + tok * H * kD;
+    // Every lane runs the same trip count (the shuffles need the whole warp).
+    for (int hb = 0; hb < H; hb += 8 * kNrRows) {
+      uint4 xv[kNrRows][4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float x0 = v[2 * q], x1 = v[2 * q + 1];
-          const float co = cs[2 * q], si = cs[2 * q + 1];
-          v[2 * q] = x0 * co - x1 * si;
-          v[2 * q + 1] = x0 * si + x1 * co;
+      for (int r = 0; r < kNrRows; ++r) {
+        const int h = hb + r * 8 + hl;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          xv[r][j] = h < H ? *reinterpret_cast<const uint4*>(xt + static_cast<int64_t>(h) * kD +
+                                                              j * 32 + sub * 8)
+                           : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int r = 0; r < kNrRows; ++r) {
+        const int h = hb + r * 8 + hl;
+        // The row stays packed (bf16) in registers: unpacked once for the sum of squares
+        // and again, a chunk at a time, for the transform.
+        float inv = 1.f;
+        if (norm) {
+          float ss = 0.f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float v[8];
+            bf16x8_to_f32(xv[r][j], v);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
+          }
+          ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+          ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+          inv = 1.f / sqrtf(ss / static_cast<float>(kD) + eps);
+        }
+        if (h >= H) continue;
+        __nv_bfloat16* yr = job.y + ((static_cast<int64_t>(b) * H + h) * T + t) * kD;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float v[8];
+          bf16x8_to_f32(xv[r][j], v);
+          if (norm) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = v[e] * inv * w[j][e];
+          }
+          if (rope) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float x0 = v[2 * q], x1 = v[2 * q + 1];
+              const float co = cs[j][2 * q], si = cs[j][2 * q + 1];
+              v[2 * q] = x0 * co - x1 * si;
+              v[2 * q + 1] = x0 * si + x1 * co;
+            }
+          }
+          *reinterpret_cast<uint4*>(yr + j * 32 + sub * 8) =
+              make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                         pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
         }
       }
-      uint4 o;
-      o.x = pack_bf16x2(v[0], v[1]);
-      o.y = pack_bf16x2(v[2], v[3]);
-      o.z = pack_bf16x2(v[4], v[5]);
-      o.w = pack_bf16x2(v[6], v[7]);
-      const size_t drow = (static_cast<size_t>(b) * H + h) * T + t;
-      *reinterpret_cast<uint4*>(job.y + drow * kD + sub * 8) = o;
-    }
-    if (++h == static_cast<uint32_t>(H)) {
-      h = 0;
-      if (++t == static_cast<uint32_t>(T)) { t = 0; ++b; }
     }
   }
 }
@@ -904,9 +927,21 @@ int launch_norm_rope(const NormRopeJob* jobs, int njobs, int B, int T, int H, fl
   const int64_t rows = static_cast<int64_t>(B) * T * H;
   if (rows == 0 || njobs == 0) return B200_OK;
   if (rows >= (int64_t{1} << 31)) return B200_ERR_INVALID;
-  const int64_t groups = (rows + kNormRows - 1) / kNormRows;  // 16 threads each
-  const int64_t blocks = (groups * 16 + 255) / 256;
-  if (blocks > 0x7fffffff) return B200_ERR_INVALID;
+  // One warp per token; enough CTAs (8 warps each) for every SM to hold several per job,
+  // the grid-stride loop takes the rest.
+  static const int64_t slots = [] {  // resident CTAs of this kernel on the whole GPU
+    int dev = 0, n = 148, c = 2;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c, norm_rope_kernel, 256, 0) != cudaSuccess ||
+        c < 1)
+      c = 1;
+    return int64_t{n} * c;
+  }();
+  const int64_t tokens = static_cast<int64_t>(B) * T;
+  const int64_t want = (tokens + 7) / 8;
+  const int64_t cap = std::max<int64_t>(1, slots * 2 / njobs);
+  const int64_t blocks = std::min(want, cap);
   NormRopeJob j[3] = {jobs[0], njobs > 1 ? jobs[1] : jobs[0], njobs > 2 ? jobs[2] : jobs[0]};
   dim3 grid(static_cast<unsigned>(blocks), njobs);
   norm_rope_kernel<<<grid, 256, 0, stream>>>(j[0], j[1], j[2], B, T, H, eps, pe, pe_bs, rope_mask,
