@@ -664,19 +664,21 @@ __global__ void __launch_bounds__(64) wait_selftest_kernel(int32_t* status, uint
 
 // ------------------------------------------------------------------ norm + RoPE
 // One warp per token (b, t) at a time (grid-stride over the B*T tokens); a group of 4
-// lanes owns one head's row of 128 values, 8 heads side by side, two rows in flight per
-// lane.  Lane `sub` of a group holds the 8-value chunks j*4 + sub (j = 0..3), so each load
-// or store instruction covers 64 contiguous bytes per row.  The token's RoPE table row
-// and the norm weights are loaded once and reused for every head.  Per row:
-// y = RoPE(x / sqrt(mean(x^2) + eps) * w) in f32, rounded to bf16 once, written
-// head-major; the sum of squares is 2 shuffles over the group.
+// lanes owns one head's row of 128 values, 8 heads side by side, four rows in flight per
+// lane (all 32 heads of a token: 8 KiB of loads per warp issued back to back).  Lane `sub`
+// of a group holds the 8-value chunks j*4 + sub (j = 0..3), so each load or store
+// instruction covers 64 contiguous bytes per row.  The token's RoPE table row is staged
+// once per warp in shared memory and the norm weights once per CTA, both reused for every
+// head.  Per row: y = RoPE(x / sqrt(mean(x^2) + eps) * w) in f32, rounded to bf16 once,
+// written head-major; the sum of squares is 2 shuffles over the group.
 struct NormRopeJob {
   const __nv_bfloat16* x;
   __nv_bfloat16* y;
   const float* w;  // NULL: no norm
 };
 
-constexpr int kNrRows = 2;  // rows (heads) in flight per lane
+constexpr int kNrRows = 4;     // rows (heads) in flight per lane
+constexpr int kNrThreads = 256;
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -687,18 +689,18 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   }
 }
 
-__device__ __forceinline__ void load_f32x8(const float* p, float (&f)[8]) {
+__device__ __forceinline__ void lds_f32x8(const float* p, float (&f)[8]) {
   const float4 a = *reinterpret_cast<const float4*>(p);
   const float4 b = *reinterpret_cast<const float4*>(p + 4);
   f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
   f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
 }
 
-__global__ void __launch_bounds__(256, 2) norm_rope_kernel(NormRopeJob j0, NormRopeJob j1,
-                                                         NormRopeJob j2, int B, int T, int H,
-                                                         float eps, const float* pe,
-                                                         int64_t pe_bs, int rope_mask,
-                                                         int32_t* zero, int n_zero) {
+__global__ void __launch_bounds__(kNrThreads, 2) norm_rope_kernel(
+    NormRopeJob j0, NormRopeJob j1, NormRopeJob j2, int B, int T, int H, float eps,
+    const float* pe, int64_t pe_bs, int rope_mask, int32_t* zero, int n_zero) {
+  __shared__ __align__(16) float s_w[kD];
+  __shared__ __align__(16) float s_pe[kNrThreads / 32][kD];
   // Also clears the attention kernel's split arrival counters (n_zero <= 256), which saves
   // a separate memset before the attention launch that follows on the same stream.
   if (zero && blockIdx.x == 0 && blockIdx.y == 0 && static_cast<int>(threadIdx.x) < n_zero)
@@ -707,24 +709,18 @@ __global__ void __launch_bounds__(256, 2) norm_rope_kernel(NormRopeJob j0, NormR
   const bool rope = pe != nullptr && ((rope_mask >> blockIdx.y) & 1);
   const bool norm = job.w != nullptr;
   const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const int sub = lane & 3;   // chunk column within the group
   const int hl = lane >> 2;   // head offset within the warp's 8
-  const int warps = gridDim.x * (blockDim.x >> 5);
-  float w[4][8];
-  if (norm) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) load_f32x8(job.w + j * 32 + sub * 8, w[j]);
-  }
+  if (norm && threadIdx.x < kD / 4)
+    reinterpret_cast<float4*>(s_w)[threadIdx.x] = reinterpret_cast<const float4*>(job.w)[threadIdx.x];
+  __syncthreads();
+  float* pe_s = s_pe[warp];
   const int64_t tokens = static_cast<int64_t>(B) * T;
-  for (int64_t tok = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       tok < tokens; tok += warps) {
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kNrThreads / 32);
+  for (int64_t tok = static_cast<int64_t>(blockIdx.x) * (kNrThreads / 32) + warp; tok < tokens;
+       tok += warps) {
     const int b = static_cast<int>(tok / T), t = static_cast<int>(tok - static_cast<int64_t>(b) * T);
-    float cs[4][8];
-    if (rope) {
-      const float* pr = pe + static_cast<int64_t>(b) * pe_bs + static_cast<int64_t>(t) * kD;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) load_f32x8(pr + j * 32 + sub * 8, cs[j]);
-    }
     const __nv_bfloat16* xt = job.x + tok * H * kD;
     // Every lane runs the same trip count (the shuffles need the whole warp).
     for (int hb = 0; hb < H; hb += 8 * kNrRows) {
@@ -737,6 +733,13 @@ __global__ void __launch_bounds__(256, 2) norm_rope_kernel(NormRopeJob j0, NormR
           xv[r][j] = h < H ? *reinterpret_cast<const uint4*>(xt + static_cast<int64_t>(h) * kD +
                                                               j * 32 + sub * 8)
                            : make_uint4(0, 0, 0, 0);
+      }
+      if (rope && hb == 0) {
+        const float4 c = reinterpret_cast<const float4*>(
+            pe + static_cast<int64_t>(b) * pe_bs + static_cast<int64_t>(t) * kD)[lane];
+        __syncwarp();  // the previous token's reads of pe_s are done
+        reinterpret_cast<float4*>(pe_s)[lane] = c;
+        __syncwarp();
       }
 #pragma unroll
       for (int r = 0; r < kNrRows; ++r) {
@@ -764,14 +767,18 @@ __global__ void __launch_bounds__(256, 2) norm_rope_kernel(NormRopeJob j0, NormR
           float v[8];
           bf16x8_to_f32(xv[r][j], v);
           if (norm) {
+            float w[8];
+            lds_f32x8(s_w + j * 32 + sub * 8, w);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = v[e] * inv * w[j][e];
+            for (int e = 0; e < 8; ++e) v[e] = v[e] * inv * w[e];
           }
           if (rope) {
+            float cs[8];
+            lds_f32x8(pe_s + j * 32 + sub * 8, cs);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const float x0 = v[2 * q], x1 = v[2 * q + 1];
-              const float co = cs[j][2 * q], si = cs[j][2 * q + 1];
+              const float co = cs[2 * q], si = cs[2 * q + 1];
               v[2 * q] = x0 * co - x1 * si;
               v[2 * q + 1] = x0 * si + x1 * co;
             }
@@ -933,7 +940,8 @@ int launch_norm_rope(const NormRopeJob* jobs, int njobs, int B, int T, int H, fl
     int dev = 0, n = 148, c = 2;
     if (cudaGetDevice(&dev) == cudaSuccess)
       cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c, norm_rope_kernel, 256, 0) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c, norm_rope_kernel, kNrThreads, 0) !=
+            cudaSuccess ||
         c < 1)
       c = 1;
     return int64_t{n} * c;
@@ -944,7 +952,7 @@ int launch_norm_rope(const NormRopeJob* jobs, int njobs, int B, int T, int H, fl
   const int64_t blocks = std::min(want, cap);
   NormRopeJob j[3] = {jobs[0], njobs > 1 ? jobs[1] : jobs[0], njobs > 2 ? jobs[2] : jobs[0]};
   dim3 grid(static_cast<unsigned>(blocks), njobs);
-  norm_rope_kernel<<<grid, 256, 0, stream>>>(j[0], j[1], j[2], B, T, H, eps, pe, pe_bs, rope_mask,
+  norm_rope_kernel<<<grid, kNrThreads, 0, stream>>>(j[0], j[1], j[2], B, T, H, eps, pe, pe_bs, rope_mask,
                                              zero, n_zero);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
