@@ -35,6 +35,8 @@ EXPORTED = (
     "b200_residual_adaln", "b200_swiglu",
     "b200_dequant_q4_k", "b200_dequant_q6_k", "b200_wait_selftest", "b200_gemm",
     "b200_gemm_scatter", "b200_reduce_gather_bf16", "b200_qkv_norm_rope_gemm",
+    "b200_tp_unique_id", "b200_tp_init", "b200_tp_init_from_nccl", "b200_tp_rank", "b200_tp_size",
+    "b200_tp_out_proj_allreduce", "b200_tp_wait", "b200_tp_destroy",
 )
 
 
@@ -97,6 +99,14 @@ def lib() -> ctypes.CDLL:
         L.b200_gemm.argtypes = [vp, i64, vp, i64, vp, i64, i32, i32, i32, i32, vp, vp]
         L.b200_gemm_scatter.argtypes = [vp, i64, vp, i64, vp, i32, i32, i32, i64, i32, i32, i32, vp, vp]
         L.b200_reduce_gather_bf16.argtypes = [vp, i32, i32, i32, i32, i64, vp, i32, i64, i64, vp]
+        L.b200_tp_unique_id.argtypes = [vp]
+        L.b200_tp_init.argtypes = [ctypes.POINTER(vp), vp, i32, i32, ctypes.c_uint32]
+        L.b200_tp_init_from_nccl.argtypes = [ctypes.POINTER(vp), vp, ctypes.c_uint32]
+        L.b200_tp_rank.argtypes = [vp]
+        L.b200_tp_size.argtypes = [vp]
+        L.b200_tp_out_proj_allreduce.argtypes = [vp, vp, ctypes.c_size_t, i32, vp]
+        L.b200_tp_wait.argtypes = [vp, vp]
+        L.b200_tp_destroy.argtypes = [vp]
         L.b200_qkv_norm_rope_gemm.argtypes = [vp, i64, vp, i32, i32, i32, i32, vp, vp, f32, vp, i64,
                                               vp, vp, vp, vp, vp]
         L.b200_strerror.argtypes = [ctypes.c_int]
@@ -454,3 +464,67 @@ def qkv_norm_rope_gemm(x, w_qkv, batch: int, tokens: int, heads: int, norm_q_w, 
                                          _dptr(pe), pe_bs, _dptr(q_rot), _dptr(k_rot), _dptr(v),
                                          _dptr(status), _stream(stream)), "b200_qkv_norm_rope_gemm")
     return q_rot, k_rot, v
+
+
+# ----------------------------------------------------------------- head-sharding communicator
+TP_ID_BYTES = 128  # B200_TP_ID_BYTES
+DTYPE_BF16, DTYPE_F32 = 0, 1
+
+
+def tp_unique_id() -> bytes:
+    """A new group id (b200_tp_unique_id), made on one rank and handed to the others."""
+    buf = (ctypes.c_uint8 * TP_ID_BYTES)()
+    _check(lib().b200_tp_unique_id(buf), "b200_tp_unique_id")
+    return bytes(buf)
+
+
+class TpComm:
+    """The b200_tp.h communicator of a head-sharded group: the per-block sum of the
+    `to_out` partials (b200_tp_out_proj_allreduce) on the caller's stream, with every host
+    wait bounded by ``timeout_ms``."""
+
+    def __init__(self, uid: bytes, world: int, rank: int, timeout_ms: int = 60000):
+        if len(uid) != TP_ID_BYTES:
+            raise ValueError(f"group id must be {TP_ID_BYTES} bytes")
+        h = ctypes.c_void_p()
+        ub = (ctypes.c_uint8 * TP_ID_BYTES).from_buffer_copy(uid)
+        _check(lib().b200_tp_init(ctypes.byref(h), ub, world, rank, timeout_ms), "b200_tp_init")
+        self._h = h
+
+    @classmethod
+    def from_group(cls, group=None, timeout_ms: int = 60000):
+        """Every rank of a torch.distributed group (any backend) calls this; rank 0's id
+        reaches the others by broadcast."""
+        import torch.distributed as dist
+        obj = [tp_unique_id() if dist.get_rank(group) == 0 else None]
+        dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group else 0,
+                                   group=group)
+        return cls(obj[0], dist.get_world_size(group), dist.get_rank(group), timeout_ms)
+
+    @property
+    def rank(self) -> int:
+        return lib().b200_tp_rank(self._h)
+
+    @property
+    def size(self) -> int:
+        return lib().b200_tp_size(self._h)
+
+    def allreduce_(self, t, stream=None):
+        """In-place sum over the group of a contiguous bf16 or f32 device tensor."""
+        import torch
+        if not t.is_contiguous():
+            raise ValueError("partial must be contiguous")
+        dt = {torch.bfloat16: DTYPE_BF16, torch.float32: DTYPE_F32}.get(t.dtype)
+        if dt is None:
+            raise ValueError("partial must be bf16 or f32")
+        _check(lib().b200_tp_out_proj_allreduce(self._h, _dptr(t), t.numel(), dt, _stream(stream)),
+               "b200_tp_out_proj_allreduce")
+        return t
+
+    def wait(self, stream=None):
+        _check(lib().b200_tp_wait(self._h, _stream(stream)), "b200_tp_wait")
+
+    def close(self):
+        if self._h:
+            h, self._h = self._h, None
+            _check(lib().b200_tp_destroy(h), "b200_tp_destroy")

@@ -61,8 +61,12 @@ def out_proj_partial(attn_local, w_out, h0: int, h1: int, head_dim: int = 128):
     return torch.matmul(attn_local, w_cols.t())
 
 
-def allreduce_sum_(t, group=None):
-    """In-place sum of `t` over the ranks of `group` (NCCL on GPUs, gloo on CPU)."""
+def allreduce_sum_(t, group=None, comm=None, stream=None):
+    """In-place sum of `t` over the ranks of `group` (NCCL on GPUs, gloo on CPU), or over
+    `comm` (a b200attn.TpComm: the C-ABI communicator, b200_tp_out_proj_allreduce on
+    `stream`) when one is given."""
+    if comm is not None:
+        return comm.allreduce_(t, stream=stream)
     import torch.distributed as dist
     if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
@@ -81,19 +85,20 @@ def max_over_ranks(value: float, device=None, group=None) -> float:
 
 def head_sharded_attention_layer(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w, pe, w_out,
                                  h0: int, h1: int, desc=None, workspace=None, group=None,
-                                 stream=None):
+                                 stream=None, comm=None):
     """One layer of head-sharded joint attention on this rank's heads [h0, h1).
 
     q, k, v: bf16 [B, T, h1-h0, D] (this rank's column slice of the projections);
     prefix_k/v: bf16 [B, h1-h0, P, D]; w_out: bf16 [hidden, H*D] (full to_out weight).
-    Returns the all-reduced to_out output [B, T, hidden] (identical on every rank).
+    Returns the all-reduced to_out output [B, T, hidden] (identical on every rank).  The
+    sum goes through `comm` (b200attn.TpComm) when given, else torch.distributed.
     """
     import b200attn
     b, t, hl, d = q.shape
     attn = b200attn.attention_forward(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w, pe,
                                       desc=desc, workspace=workspace, stream=stream)
     partial = out_proj_partial(attn.reshape(b * t, hl * d), w_out, h0, h1, d)
-    allreduce_sum_(partial, group)
+    allreduce_sum_(partial, group, comm=comm, stream=stream)
     return partial.reshape(b, t, -1)
 
 

@@ -15,11 +15,12 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "b200attn", "libb200attn.so")
-SOURCES = ["attn_fwd.cu", "block_ops.cu", "dequant.cu", "gemm.cu", "host_layout.cpp"]
+SOURCES = ["attn_fwd.cu", "block_ops.cu", "dequant.cu", "gemm.cu", "host_layout.cpp", "tp.cpp"]
 HEADERS = ["ptx.cuh", os.path.join("..", "..", "include", "b200_attn.h"),
            os.path.join("..", "..", "include", "b200_block_ops.h"),
            os.path.join("..", "..", "include", "b200_gguf.h"),
-           os.path.join("..", "..", "include", "b200_gemm.h")]
+           os.path.join("..", "..", "include", "b200_gemm.h"),
+           os.path.join("..", "..", "include", "b200_tp.h")]
 
 
 def nvcc() -> str:
@@ -47,7 +48,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         "-std=c++17", "-Xcompiler", "-fPIC,-O3", "-shared", "-cudart", "static",
         "-Xptxas", "-v", "-I", os.path.join(ROOT, "include"),
         "-o", LIB,
-    ] + [os.path.join(CSRC, s) for s in SOURCES]
+    ] + [os.path.join(CSRC, s) for s in SOURCES] + ["-ldl"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     with open(os.path.join(HERE, "_build", "ptxas.log"), "w") as f:
         f.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)

@@ -18,7 +18,7 @@ GOLDEN = os.path.join(ROOT, "tests", "golden")
 
 def declared_functions():
     names = set()
-    for hdr in ("b200_attn.h", "b200_block_ops.h", "b200_gguf.h", "b200_gemm.h"):
+    for hdr in sorted(f for f in os.listdir(os.path.join(ROOT, "include")) if f.endswith(".h")):
         src = open(os.path.join(ROOT, "include", hdr)).read()
         src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
         names |= set(re.findall(r"\b(b200_[a-z0-9_]+)\s*\(", src))
@@ -159,3 +159,30 @@ def test_block_causal_limits_match_the_reference_mask(text, cond):
     assert want is not None
     assert np.array_equal(b200attn.block_causal_limits(ids), want)
     assert np.all(np.diff(want) >= 0)  # non-decreasing: the kernel relies on it
+
+
+def test_tp_entry_points_reject_bad_arguments():
+    lib = b200attn.lib()
+    h = ctypes.c_void_p()
+    uid = (ctypes.c_uint8 * b200attn.TP_ID_BYTES)()
+    assert lib.b200_tp_unique_id(None) == b200attn.ERR_INVALID
+    assert lib.b200_tp_init(None, uid, 1, 0, 0) == b200attn.ERR_INVALID
+    assert lib.b200_tp_init(ctypes.byref(h), None, 1, 0, 0) == b200attn.ERR_INVALID
+    assert lib.b200_tp_init(ctypes.byref(h), uid, 2, 2, 0) == b200attn.ERR_INVALID  # rank >= n
+    assert lib.b200_tp_init(ctypes.byref(h), uid, 0, 0, 0) == b200attn.ERR_INVALID
+    assert lib.b200_tp_init_from_nccl(ctypes.byref(h), None, 0) == b200attn.ERR_INVALID
+    assert lib.b200_tp_out_proj_allreduce(None, None, 1, 0, None) == b200attn.ERR_INVALID
+    assert lib.b200_tp_wait(None, None) == b200attn.ERR_INVALID
+    assert lib.b200_tp_destroy(None) == b200attn.ERR_INVALID
+    assert lib.b200_tp_rank(None) == b200attn.ERR_INVALID
+    assert lib.b200_tp_size(None) == b200attn.ERR_INVALID
+
+
+def test_tp_unique_id_is_fresh():
+    """Group ids come from NCCL at run time (no link-time NCCL dependency); two calls give
+    two groups."""
+    try:
+        a, b = b200attn.tp_unique_id(), b200attn.tp_unique_id()
+    except b200attn.B200Error as e:
+        pytest.skip(f"NCCL not loadable here: {e}")
+    assert len(a) == b200attn.TP_ID_BYTES and a != b
