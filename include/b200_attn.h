@@ -245,8 +245,10 @@ int b200_key_valid_to_desc(const uint8_t* key_valid, int32_t batch, int32_t pref
  */
 int b200_block_causal_limits(const int64_t* image_ids, int32_t len, int32_t* limits_out);
 
-/* Human-readable text of a b200_status. */
+/* Human-readable text of a b200_status; b200_attn_strerror is the same function under
+ * the name the engine's binding plan uses. */
 const char* b200_strerror(int status);
+const char* b200_attn_strerror(int status);
 
 /* ABI version (B200_ATTN_ABI_VERSION). */
 int b200_abi_version(void);

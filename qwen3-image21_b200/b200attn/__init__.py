@@ -31,7 +31,7 @@ EXPORTED = (
     "b200_norm_rope", "b200_qk_norm_rope",
     "b200_joint_layout", "b200_rope_positions", "b200_rope_pe", "b200_key_valid_to_desc",
     "b200_block_causal_limits",
-    "b200_strerror", "b200_abi_version",
+    "b200_strerror", "b200_attn_strerror", "b200_abi_version",
     "b200_residual_adaln", "b200_swiglu",
     "b200_dequant_q4_k", "b200_dequant_q6_k", "b200_wait_selftest", "b200_gemm",
     "b200_gemm_scatter", "b200_reduce_gather_bf16", "b200_qkv_norm_rope_gemm",
@@ -111,6 +111,7 @@ def lib() -> ctypes.CDLL:
                                               vp, vp, vp, vp, vp]
         L.b200_strerror.argtypes = [ctypes.c_int]
         L.b200_strerror.restype = ctypes.c_char_p
+        L.b200_attn_strerror.restype = ctypes.c_char_p
         for name in EXPORTED:
             if name != "b200_strerror":
                 getattr(L, name).restype = ctypes.c_int

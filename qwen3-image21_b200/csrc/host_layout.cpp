@@ -226,4 +226,6 @@ extern "C" const char* b200_strerror(int status) {
   }
 }
 
+extern "C" const char* b200_attn_strerror(int status) { return b200_strerror(status); }
+
 extern "C" int b200_abi_version(void) { return B200_ATTN_ABI_VERSION; }
