@@ -176,6 +176,16 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- reference
+def attn_step_config(cfg, L, world):
+    """The `config` of the attention-step configs (1-3), shared by both arms."""
+    T = cfg["grid"][0] * cfg["grid"][1]
+    return {"workload": cfg["name"] + ", attention of 32 blocks per step",
+            "T": T, "P": cfg["P"], "prefix_valid": cfg["pv"] if cfg["pv"] is not None else cfg["P"],
+            "heads": HEADS, "head_dim": HEAD_DIM, "blocks_per_step": L, "batch": 1,
+            "parallelism": f"dp{world} (independent generations)",
+            "l2": "inputs exceed L2 (3.3 GB of per-block q/k/v/prefix per step)"}
+
+
 def run_reference(args, rank):
     """The CPU restatement of the reference's chunked attention, timed on the host."""
     if rank != 0:
@@ -210,8 +220,7 @@ def run_reference(args, rank):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
-        "config": {"workload": f"{cfg['name']} sample", "T": t, "P": cfg["P"], "heads": heads,
-                   "head_dim": HEAD_DIM},
+        "config": attn_step_config(cfg, args.layers or cfg["layers"], args.gpus),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -252,6 +261,8 @@ def main():
     if args.impl == "reference":
         if args.config == "c5":
             run_reference_denoise(args, rank)
+        elif args.config == "c4":
+            run_reference_head_sharded(args, rank)
         else:
             run_reference(args, rank)
         return
@@ -414,11 +425,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) q/k/v and prefix cache, weight-1 norms)",
-            "config": {"workload": cfg["name"] + ", attention of 32 blocks per step",
-                       "T": T, "P": P, "prefix_valid": cfg["pv"] if cfg["pv"] is not None else P,
-                       "heads": HEADS, "head_dim": HEAD_DIM, "blocks_per_step": L, "batch": 1,
-                       "parallelism": f"dp{world} (independent generations)",
-                       "l2": "inputs exceed L2 (3.3 GB of per-block q/k/v/prefix per step)"},
+            "config": attn_step_config(cfg, L, world),
             "pct_bf16_peak": 100.0 * value / world / peak,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
@@ -438,6 +445,67 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+C4_METRIC = "block TFLOP/s at 2048^2, head-sharded (attention + to_out + all-reduce)"
+
+
+def c4_config(cfg, world):
+    """The `config` of config 4, shared by both arms."""
+    return {"workload": cfg["name"] + ", one block per step",
+            "T": cfg["grid"][0] * cfg["grid"][1], "P": cfg["P"],
+            "heads_per_gpu": HEADS // world, "head_dim": HEAD_DIM, "hidden": cfg["hidden"],
+            "parallelism": f"heads/{world}; to_out partials summed over the ranks",
+            "l2": "inputs exceed L2"}
+
+
+def run_reference_head_sharded(args, rank):
+    """Config 4 on the host cores: the C port of chunked_attention for a sample of heads and
+    their share of to_out (numpy f32 GEMM), at the B200 arm's metric (block TFLOP/s)."""
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle import cpu as ocpu  # CPU baseline leg (test / baseline infrastructure)
+    cfg = CONFIGS["c4"]
+    heads = max(1, min(args.cpu_heads, HEADS))
+    t = cfg["grid"][0] * cfg["grid"][1]
+    t_s = 2048  # query rows of the sample (of 16384), all keys
+    rng = np.random.default_rng(9)
+    bits = lambda shape: (rng.standard_normal(shape, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    q = bits((1, t_s, heads, HEAD_DIM))
+    k, v = (bits((1, t, heads, HEAD_DIM)) for _ in range(2))
+    pk, pv = (bits((1, heads, cfg["P"], HEAD_DIM)) for _ in range(2))
+    w = np.ones(HEAD_DIM, np.float32)
+    pe = np.tile(np.array([1.0, 0.0], np.float32), (t, HEAD_DIM // 2))
+    w_out = (0.02 * rng.standard_normal((cfg["hidden"], heads * HEAD_DIM))).astype(np.float32)
+    threads = os.cpu_count() or 1
+
+    def one():
+        # a t_s-token slice of the call (its queries, keys and values) against the prefix
+        o = ocpu.attention_forward(q, k[:, :t_s], v[:, :t_s], pk, pv, w, w, 1e-6, pe[:t_s],
+                                   None, HEAD_DIM ** -0.5, threads)
+        return np.asarray(o, np.float32).reshape(t_s, heads * HEAD_DIM) @ w_out.T
+
+    for _ in range(min(args.warmup, 1)):
+        one()
+    n = max(1, min(args.steps, 3))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        one()
+    dt = (time.perf_counter() - t0) / n
+    flops = 4.0 * heads * t_s * (t_s + cfg["P"]) * HEAD_DIM + 2.0 * t_s * heads * HEAD_DIM * cfg["hidden"]
+    value = flops / dt / 1e12
+    sample = (f"{heads} of 32 heads, {t_s} of {t} query rows against {t_s} + {cfg['P']} keys, "
+              f"with their to_out share (oracle C port + numpy f32 GEMM), per step")
+    print(json.dumps({
+        "impl": "reference", "metric": C4_METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": n, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1))", "config": c4_config(cfg, args.gpus),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
 
 
 def run_head_sharded(args, cfg, rank, world, dev):
@@ -550,18 +618,15 @@ def run_head_sharded(args, cfg, rank, world, dev):
         peak = float(pk_d.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
         achieved = attn_flops * hl / HEADS / (attn_ms / 1e3) / 1e12
         line = {
-            "metric": "block TFLOP/s at 2048^2, head-sharded (attention + to_out + all-reduce)",
+            "metric": C4_METRIC,
             "value": (attn_flops + proj_flops) / (ms_step / 1e3) / 1e12, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) q/k/v and prefix cache, N(0,0.02) to_out)",
-            "config": {"workload": cfg["name"] + ", one block per step", "T": T, "P": P,
-                       "heads_per_gpu": hl, "head_dim": HEAD_DIM, "hidden": hidden,
-                       "parallelism": (f"heads/{world}; to_out partials summed by "
-                                       + (fused_note if use_fused else
-                                          "cuBLAS + NCCL all-reduce (faster than the fused "
-                                          "path at this rank count)")),
-                       "l2": "inputs exceed L2"},
+            "config": c4_config(cfg, world),
+            "sum_of_partials": (fused_note if use_fused else
+                                "cuBLAS + NCCL all-reduce (faster than the fused path at this "
+                                "rank count)"),
             "nccl_path": {"ms_per_step": ms_nccl,
                           "value": (attn_flops + proj_flops) / (ms_nccl / 1e3) / 1e12,
                           "how": "cuBLAS to_out partial + NCCL all-reduce (bf16)"},
@@ -589,6 +654,25 @@ def c5_workload(cfg):
     rng = np.random.default_rng(5)
     lo, hi = cfg["len_range"]
     return [(int(a), int(b)) for a, b in rng.integers(lo, hi + 1, size=(cfg["prompts"], 2))]
+
+
+def c5_config(cfg, args, world):
+    """The `config` of config 5, shared by both arms."""
+    mcfg_ = None
+    try:
+        from b200attn import mmdit
+        mcfg_ = mmdit.MMDiTConfig()
+    except ImportError:
+        pass
+    return {"workload": cfg["name"], "T": cfg["grid"][0] * cfg["grid"][1],
+            "prompts": cfg["prompts"], "sequences": 2 * cfg["prompts"],
+            "prompt_lengths": c5_workload(cfg),
+            "blocks": args.layers or cfg["layers"], "hidden": getattr(mcfg_, "hidden", 4096),
+            "ffn": getattr(mcfg_, "ffn", 12288), "weights": args.weights,
+            "cfg_scale": cfg["cfg_scale"],
+            "gemm": args.gemm + (" + fused QKV/norm/RoPE" if args.fused_qkv else ""),
+            "parallelism": f"dp{world} by prompt (pos/neg pairs together)",
+            "l2": "every step streams GBs of weights and activations (> L2)"}
 
 
 def c5_flops(model_cfg, lengths, T):
@@ -713,15 +797,8 @@ def run_denoise(args, cfg, rank, world, dev):
             "data": "synthetic (random-init N(0,0.02) weights"
                     + (" quantised to GGUF Q4_K_M" if args.weights == "q4_k_m" else " in bf16")
                     + ", seeded N(0,1) prompt embeddings and noise)",
-            "config": {"workload": cfg["name"], "T": T, "prompts": cfg["prompts"],
-                       "sequences": 2 * cfg["prompts"], "prompt_lengths": pairs,
-                       "blocks": mcfg.layers, "hidden": mcfg.hidden, "ffn": mcfg.ffn,
-                       "weights": (f"{args.weights}: block linears {wbytes / 1e9:.2f} GB "
-                                   f"(7.1 B parameters)"),
-                       "cfg_scale": cfg["cfg_scale"],
-                       "gemm": args.gemm + (" + fused QKV/norm/RoPE" if args.fused_qkv else ""),
-                       "parallelism": f"dp{world} by prompt (pos/neg pairs together)",
-                       "l2": "every step streams GBs of weights and activations (> L2)"},
+            "config": c5_config(cfg, args, world),
+            "weight_bytes": {"block_linears": wbytes, "note": "7.1 B parameters"},
             "step_tflops": (lin_f + attn_f) / (ms_step / 1e3) / 1e12,
             "pct_bf16_peak": 100.0 * (lin_f + attn_f) / world / (ms_step / 1e3) / 1e12 / peak,
             "attention_ms_per_step": attn_ms, "attention_share": attn_ms / ms_step,
@@ -798,7 +875,7 @@ def run_reference_denoise(args, rank):
         "n_gpus": args.gpus, "steps": len(samples), "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (random-init weights, seeded embeddings and noise)",
-        "config": {"workload": cfg["name"] + " sample", "T": cfg["grid"][0] * cfg["grid"][1]},
+        "config": c5_config(cfg, args, args.gpus),
         "cpu_baseline": {"value": ms, "unit": "ms", "cores": os.cpu_count() or 1, "kind": "port",
                          "sample": sample},
         "e2e": {"value": ms, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
