@@ -64,6 +64,13 @@ def prompt_layout(cfg):
     slots += [False] * (other - used)
     return len(slots), slots, cond
 METRIC = "attn TFLOP/s at 1024^2 (config 2), 32 blocks per denoising step"
+
+
+def attn_metric(config: str) -> str:
+    """Metric name of the attention-step configs; config 2 is the headline."""
+    if config == "c2":
+        return METRIC
+    return f"attn TFLOP/s, {CONFIGS[config]['name']}, 32 blocks per denoising step"
 FALLBACK_PEAKS = dict(bf16_tflops=1590.0, bf16_tflops_sustained=1400.0, hbm_gbs=6650.0)
 
 
@@ -216,7 +223,7 @@ def run_reference(args, rank):
     value = flops_per_call(cfg, heads) / dt / 1e12
     sample = f"1 of 32 blocks, {heads} of 32 heads of {cfg['name']} per step (oracle C port, f32)"
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "impl": "reference", "metric": attn_metric(args.config), "value": value, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
@@ -421,7 +428,7 @@ def main():
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(cfg, max(1, min(args.cpu_heads, HEADS)))
         line = {
-            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "metric": attn_metric(args.config), "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) q/k/v and prefix cache, weight-1 norms)",
