@@ -4,10 +4,12 @@
 A step is the attention of one cached denoising step across all 32 MMDiT blocks at
 1024^2 text-to-image (config 2): per block, 4096 image-token queries attend over the
 block's 512-token prefix KV cache plus the step's 4096 image keys, 32 heads x 128, bf16.
-Each block call is the public path's two launches — the Q/K RMSNorm+RoPE prologue and
-the tcgen05 attention kernel (exactly what b200_attn_fwd launches) — with CUDA events
-around the attention launch for the roofline.  ``e2e`` runs the same step through
-b200_attn_fwd with host (pinned) q/k/v copied in and the output copied out per block.
+Each block call is the public b200_attn_fwd (two launches: the Q/K RMSNorm+RoPE prologue
+and the tcgen05 attention kernel); the timed region replays the step's 32 calls as one CUDA
+graph (``--no-graph``: called one by one).  Right after it, under the same clock sampling,
+the same step runs with the two launches called separately and CUDA events around every
+attention launch: the roofline's kernel time.  ``e2e`` runs the step through b200_attn_fwd
+with host (pinned) q/k/v copied in and the output copied out per block.
 
 Multi-GPU (torchrun, one process per GPU): independent generations, data-parallel, no
 collective on the data path (weak scaling); the barrier and a max-reduction of the
@@ -86,6 +88,9 @@ def parse_args():
                     help="blocks per step (default 32; fewer only for profiling runs)")
     ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="configs 1-3: launch the step's calls one by one instead of replaying "
+                         "them as one CUDA graph")
     ap.add_argument("--weights", choices=["q4_k_m", "bf16"], default="q4_k_m",
                     help="config 5: block linears as GGUF Q4_K_M blocks (the config) or bf16")
     ap.add_argument("--prompts", type=int, default=None,
@@ -319,15 +324,26 @@ def main():
     split_ws = torch.empty(b200attn.SPLIT_WORKSPACE_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def step(marks=None):
+    fwd_ws = torch.empty(2 * T * HEADS * HEAD_DIM * 2 + b200attn.SPLIT_WORKSPACE_BYTES + 512,
+                         dtype=torch.uint8, device=dev)
+
+    def step(s):
+        """One denoising step's attention through the public call (b200_attn_fwd: the
+        norm/RoPE prologue, then the attention kernel), block after block."""
+        for ly in layers:
+            b200attn.attention_forward(ly["q"], ly["k"], ly["v"], ly["pk"], ly["pv"], ones, ones,
+                                       pe, desc=desc, out=out, workspace=fwd_ws, status=status,
+                                       stream=s)
+
+    def step_marked(marks):
+        """The same step as b200_attn_fwd's two launches called one by one, with CUDA events
+        around every attention launch (the roofline's kernel time)."""
         for li, ly in enumerate(layers):
             b200attn.qk_norm_rope(ly["q"], ly["k"], ones, ones, 1e-6, pe, q_rot, k_rot, stream=stream)
-            if marks is not None:
-                marks[li][0].record(stream)
+            marks[li][0].record(stream)
             b200attn.joint_attention(q_rot, k_rot, ly["v"], ly["pk"], ly["pv"], desc=desc, out=out,
                                      workspace=split_ws, status=status, stream=stream)
-            if marks is not None:
-                marks[li][1].record(stream)
+            marks[li][1].record(stream)
 
     def barrier():
         if world > 1:
@@ -335,18 +351,39 @@ def main():
         torch.cuda.synchronize(dev)
 
     for _ in range(args.warmup):
-        step()
+        step(stream)
     barrier()
+    graph = None
+    if not args.no_graph:
+        # The whole step as one CUDA graph: the host work of the 32 calls (argument checks,
+        # tensor maps) happens once at capture, and replay launches the kernels back to back.
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            step(side)
+        stream.wait_stream(side)
+        for _ in range(args.warmup):
+            graph.replay()
+        barrier()
+    n_marked = max(1, min(args.steps, 20))
     marks = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L)]
-             for _ in range(args.steps)]
+             for _ in range(n_marked)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
     with ClockSampler(uuid) as clocks:
         barrier()
         start.record(stream)
-        for s in range(args.steps):
-            step(marks[s])
+        for _ in range(args.steps):
+            if graph is not None:
+                graph.replay()
+            else:
+                step(stream)
         end.record(stream)
+        barrier()
+        # the attention kernel's launch time, same kernels and inputs, under the same clocks
+        for s in range(n_marked):
+            step_marked(marks[s])
         barrier()
     ms_total = start.elapsed_time(end)
     attn_ms = [m[0].elapsed_time(m[1]) for st in marks for m in st]
@@ -447,6 +484,8 @@ def main():
                          "copies on their own streams, double-buffered against the attention")},
             "clocks": clocks.summary(),
             "gpu_launches": args.steps * L * 2,
+            "launch": ("one CUDA graph per step (32 b200_attn_fwd calls captured once, replayed)"
+                       if graph is not None else "b200_attn_fwd called block by block"),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
