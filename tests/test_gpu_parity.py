@@ -195,6 +195,39 @@ def test_attention_forward_is_deterministic_and_status_clear(cuda):
     assert int(status.item()) == 0
 
 
+def test_attention_forward_replays_in_a_cuda_graph(cuda):
+    """b200_attn_fwd captured in a CUDA graph (as the benchmark replays a step) gives the
+    eager call's output on every replay, with new inputs copied into the captured buffers
+    (the tail split's counters reset themselves between replays)."""
+    torch = _torch()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    H = (sms + 3 + 1) // 2  # T = 512: 2 query blocks per head, a last wave to split
+    d, h = make_case(1, 512, H, 256, 91, cuda, pv=[200])
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = torch.empty(1, 512, H * 128, dtype=torch.bfloat16, device=cuda)
+    args = b200attn.make_args(d["q"], d["k"], d["v"], d["pk"], d["pv"], d["wq"], d["wk"], d["pe"],
+                              out, d["desc"])
+    ws = torch.empty(b200attn.workspace_bytes(args), dtype=torch.uint8, device=cuda)
+    eager = run_gpu(d, workspace=ws, status=status).clone()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        run_gpu(d, out=out, workspace=ws, status=status, stream=side)
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(3):
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+    d2, h2 = make_case(1, 512, H, 256, 92, cuda, pv=[200])
+    for name in ("q", "k", "v", "pk", "pv", "wq", "wk"):
+        d[name].copy_(d2[name])
+    graph.replay()
+    torch.cuda.synchronize()
+    check(f32np(out), run_oracle(h2)[0])
+    assert int(status.item()) == 0
+
+
 # ------------------------------------------------------------------ full sizes
 def _sampled_rows_check(out, h, rows):
     """Oracle on a subset of query rows (attention rows are independent)."""
