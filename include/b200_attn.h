@@ -160,6 +160,19 @@ int b200_joint_attention(const void* q_rot, const void* k_rot, const void* v,
                          b200_stream_t stream);
 
 /*
+ * The FA2 branch's contract on [B,S,H,D] tensors: out = softmax(q k^T * scale [masked]) v
+ * with token-major q [B,Sq,H,D], k, v [B,Skv,H,D] and out [B,Sq,H,D] (all bf16), no
+ * transposes.  Replaces flash_attention / candle_flash_attn::flash_attn(q, k, v, scale,
+ * causal = false) (src/transformer.rs:243-254), whose tensors have this layout.  key_len
+ * (device int32 [B] or NULL): batch row b attends to keys [0, key_len[b]).  One kernel on
+ * `stream`; no workspace, no host sync.
+ */
+int b200_flash_attention(const void* q, const void* k, const void* v, void* out,
+                         int32_t batch, int32_t sq, int32_t skv, int32_t heads,
+                         int32_t head_dim, float scale, const int32_t* key_len,
+                         int32_t* status, b200_stream_t stream);
+
+/*
  * Plain attention on [B,H,S,D] tensors: out = softmax(q k^T * scale [masked]) v.
  * Replaces chunked_attention(q, k, v, scale, mask) (src/transformer.rs:259-296) and
  * its flash_attention branch (src/transformer.rs:243-254) for a mask of the form

@@ -50,6 +50,8 @@ struct AttnParams {
   int32_t P;                 // rows of segment 0 (prefix cache), 0 = none
   int32_t L1;                // rows of segment 1 (this call's keys)
   int32_t v1_token_major;    // segment-1 V map is [B,T,H,D] (coords d, h, row, b)
+  int32_t k1_token_major;    // segment-1 K map is [B,T,H,D] (coords d, h, row, b)
+  int32_t q_token_major;     // Q map is [B,T,H,D] (coords d, h, row, b)
   const int32_t* seg0_len;   // valid keys of segment 0 per batch row (stride seg0_stride)
   const int32_t* seg1_len;
   int32_t seg0_stride, seg1_stride;
@@ -316,9 +318,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mbar_expect_tx(q_full, kQTiles * kTileBytes);
       for (int t = 0; t < kQTiles; ++t)
-        for (int c = 0; c < 2; ++c)
-          tma_load_4d(sQ + t * kTileBytes + c * kRegionBytes, &tm_q, q_full, c * 64,
-                      q0 + t * kBM, h, b);
+        for (int c = 0; c < 2; ++c) {
+          uint8_t* dst = sQ + t * kTileBytes + c * kRegionBytes;
+          if (p.q_token_major)
+            tma_load_4d(dst, &tm_q, q_full, c * 64, h, q0 + t * kBM, b);
+          else
+            tma_load_4d(dst, &tm_q, q_full, c * 64, q0 + t * kBM, h, b);
+        }
       bool ok = true;
       for (int j = 0; j < n && ok; ++j) {
         const int s = j & 1;
@@ -331,9 +337,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         mbar_expect_tx(k_full + s, kTileBytes);
-        for (int c = 0; c < 2; ++c)
-          tma_load_4d(sK + s * kTileBytes + c * kRegionBytes, seg0 ? &tm_k0 : &tm_k1,
-                      k_full + s, c * 64, row, h, b);
+        for (int c = 0; c < 2; ++c) {
+          uint8_t* dst = sK + s * kTileBytes + c * kRegionBytes;
+          if (!seg0 && p.k1_token_major)
+            tma_load_4d(dst, &tm_k1, k_full + s, c * 64, h, row, b);
+          else
+            tma_load_4d(dst, seg0 ? &tm_k0 : &tm_k1, k_full + s, c * 64, row, h, b);
+        }
         if (j >= kStages && !wait_or_abort(v_empty + s, (u - 1) & 1, abort_flag)) {
           ok = false;
           break;
@@ -1105,6 +1115,40 @@ extern "C" int b200_chunked_attention(const void* q, const void* k, const void* 
   prm.out_sb = static_cast<int64_t>(heads) * sq * kD;
   prm.out_sh = static_cast<int64_t>(sq) * kD;
   prm.out_sr = kD;
+  prm.status = status;
+  return launch_attention(mq, mk0, mv0, mk1, mv1, prm, batch, heads, sq, (skv + kBN - 1) / kBN,
+                          nullptr, static_cast<cudaStream_t>(stream_));
+}
+
+extern "C" int b200_flash_attention(const void* q, const void* k, const void* v, void* out,
+                                    int32_t batch, int32_t sq, int32_t skv, int32_t heads,
+                                    int32_t head_dim, float scale, const int32_t* key_len,
+                                    int32_t* status, b200_stream_t stream_) {
+  if (head_dim != kD) return B200_ERR_UNSUPPORTED;
+  if (batch <= 0 || heads <= 0 || sq < 0 || skv <= 0) return B200_ERR_INVALID;
+  if (sq == 0) return B200_OK;
+  if (!q || !k || !v || !out) return B200_ERR_INVALID;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return B200_ERR_INVALID;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return B200_ERR_INVALID;
+  CUtensorMap mq{}, mk0{}, mv0{}, mk1{}, mv1{};
+  int rc;
+  if ((rc = make_map(&mq, q, batch, heads, sq, false)) != B200_OK) return rc;
+  if ((rc = make_map(&mk1, k, batch, heads, skv, false)) != B200_OK) return rc;
+  if ((rc = make_map(&mv1, v, batch, heads, skv, false)) != B200_OK) return rc;
+  AttnParams prm{};
+  prm.T = sq;
+  prm.P = 0;
+  prm.L1 = skv;
+  prm.q_token_major = 1;
+  prm.k1_token_major = 1;
+  prm.v1_token_major = 1;
+  prm.seg1_len = key_len;
+  prm.seg1_stride = 1;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.out_sb = static_cast<int64_t>(sq) * heads * kD;
+  prm.out_sh = kD;
+  prm.out_sr = static_cast<int64_t>(heads) * kD;
   prm.status = status;
   return launch_attention(mq, mk0, mv0, mk1, mv1, prm, batch, heads, sq, (skv + kBN - 1) / kBN,
                           nullptr, static_cast<cudaStream_t>(stream_));

@@ -129,6 +129,17 @@ def test_entry_points_reject_bad_arguments_without_device():
     # misaligned (but non-null) pointers are refused before any device access
     assert lib.b200_chunked_attention(8, 16, 32, 48, 1, 1, 4, 4, 128, 0.1, None, None,
                                       None) == b200attn.ERR_INVALID
+    # the [B,S,H,D] (flash_attn) contract: same checks before any launch
+    assert lib.b200_flash_attention(None, None, None, None, 1, 4, 4, 1, 128, 0.1, None, None,
+                                    None) == b200attn.ERR_INVALID
+    assert lib.b200_flash_attention(16, 16, 16, 16, 1, 4, 4, 1, 64, 0.1, None, None,
+                                    None) == b200attn.ERR_UNSUPPORTED
+    assert lib.b200_flash_attention(16, 16, 16, 16, 1, 4, 0, 1, 128, 0.1, None, None,
+                                    None) == b200attn.ERR_INVALID
+    assert lib.b200_flash_attention(16, 16, 16, 16, 1, 0, 4, 1, 128, 0.1, None, None,
+                                    None) == b200attn.OK  # nothing to do
+    assert lib.b200_flash_attention(16, 16, 16, 16, 1, 4, 4, 1, 128, -1.0, None, None,
+                                    None) == b200attn.ERR_INVALID
 
 
 def test_workspace_bytes():

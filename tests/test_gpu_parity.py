@@ -111,6 +111,33 @@ def test_chunked_attention_matches_oracle(cuda, B, H, sq, skv):
     check(f32np(out), want)
 
 
+@pytest.mark.parametrize("B,H,sq,skv,lens", [
+    (1, 2, 256, 256, None), (2, 3, 37, 300, None), (1, 4, 500, 1000, None),
+    (2, 2, 300, 4608, [4608, 4581]),   # config-2-like key count, one row's tail padded
+    (3, 1, 129, 200, [1, 128, 200]),
+])
+def test_flash_attention_bshd_matches_oracle(cuda, B, H, sq, skv, lens):
+    """The flash_attn contract on token-major [B,S,H,D] tensors against the oracle's
+    chunked_attention on the same values transposed to [B,H,S,D]."""
+    torch = _torch()
+    g = torch.Generator().manual_seed(B * 11 + H * 7 + sq + skv)
+    q = bf16(torch.randn(B, sq, H, 128, generator=g))
+    k = bf16(torch.randn(B, skv, H, 128, generator=g))
+    v = bf16(torch.randn(B, skv, H, 128, generator=g))
+    key_len = None if lens is None else torch.tensor(lens, dtype=torch.int32, device=cuda)
+    out = b200attn.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), 128 ** -0.5,
+                                   key_len=key_len)
+    torch.cuda.synchronize()
+    mask = None
+    if lens is not None:
+        mask = np.zeros((B, 1, 1, skv), bool)
+        for b, n in enumerate(lens):
+            mask[b, ..., :n] = True
+    t = lambda x: np.transpose(f32np(x), (0, 2, 1, 3))
+    want = ref.chunked_attention(t(q), t(k), t(v), 128 ** -0.5, mask)
+    check(np.transpose(f32np(out), (0, 2, 1, 3)), want)
+
+
 def test_chunked_attention_key_mask(cuda):
     torch = _torch()
     g = torch.Generator().manual_seed(5)
