@@ -510,10 +510,26 @@ def run_reference_head_sharded(args, rank):
     their share of to_out (numpy f32 GEMM), at the B200 arm's metric (block TFLOP/s)."""
     if rank != 0:
         return
+    value, dt, n, threads, sample = c4_cpu_sample(args.cpu_heads, args.warmup, args.steps)
+    print(json.dumps({
+        "impl": "reference", "metric": C4_METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": n, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1))", "config": c4_config(CONFIGS["c4"], args.gpus),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def c4_cpu_sample(cpu_heads, warmup, steps):
+    """The oracle C port of chunked_attention on a bounded sample of config 4 plus the
+    sample's share of to_out (numpy f32 GEMM); returns (TFLOP/s, s per step, steps,
+    threads, description)."""
     import numpy as np
     from oracle import cpu as ocpu  # CPU baseline leg (test / baseline infrastructure)
     cfg = CONFIGS["c4"]
-    heads = max(1, min(args.cpu_heads, HEADS))
+    heads = max(1, min(cpu_heads, HEADS))
     t = cfg["grid"][0] * cfg["grid"][1]
     t_s = 2048  # query rows of the sample (of 16384), all keys
     rng = np.random.default_rng(9)
@@ -532,26 +548,17 @@ def run_reference_head_sharded(args, rank):
                                    None, HEAD_DIM ** -0.5, threads)
         return np.asarray(o, np.float32).reshape(t_s, heads * HEAD_DIM) @ w_out.T
 
-    for _ in range(min(args.warmup, 1)):
+    for _ in range(min(warmup, 1)):
         one()
-    n = max(1, min(args.steps, 3))
+    n = max(1, min(steps, 3))
     t0 = time.perf_counter()
     for _ in range(n):
         one()
     dt = (time.perf_counter() - t0) / n
     flops = 4.0 * heads * t_s * (t_s + cfg["P"]) * HEAD_DIM + 2.0 * t_s * heads * HEAD_DIM * cfg["hidden"]
-    value = flops / dt / 1e12
     sample = (f"{heads} of 32 heads, {t_s} of {t} query rows against {t_s} + {cfg['P']} keys, "
               f"with their to_out share (oracle C port + numpy f32 GEMM), per step")
-    print(json.dumps({
-        "impl": "reference", "metric": C4_METRIC, "value": value, "unit": "TFLOP/s",
-        "n_gpus": args.gpus, "steps": n, "warmup": args.warmup, "ms_per_step": dt * 1e3,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded N(0,1))", "config": c4_config(cfg, args.gpus),
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                         "sample": sample},
-        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    return flops / dt / 1e12, dt, n, threads, sample
 
 
 def run_head_sharded(args, cfg, rank, world, dev):
@@ -653,8 +660,65 @@ def run_head_sharded(args, cfg, rank, world, dev):
     ms_nccl = timed(step_nccl, args.steps)
     if int(status.item()) != 0:
         raise RuntimeError(f"device wait ran out during the bench (status {int(status.item())})")
+    # ---- end to end through the public calls with host buffers: this rank's q/k/v of a
+    # block copied in (host-to-device stream), b200_attn_fwd + to_out + the sum of the
+    # partials on the compute stream, the block's output copied out (device-to-host
+    # stream), double-buffered across steps.
+    e2e = None
+    if args.e2e_steps > 0:
+        host_in = dict(q=q.cpu().pin_memory(), k=k.cpu().pin_memory(), v=v.cpu().pin_memory())
+        dev_in = [dict(q=torch.empty_like(q), k=torch.empty_like(k), v=torch.empty_like(v))
+                  for _ in range(2)]
+        host_out = [torch.empty(T, hidden, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        gemm_out = [torch.empty(T, hidden, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        fwd_ws = torch.empty(2 * T * hl * HEAD_DIM * 2 + b200attn.SPLIT_WORKSPACE_BYTES + 512,
+                             dtype=torch.uint8, device=dev)
+        h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        landed, computed, drained = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
+
+        def e2e_step(i):
+            sl = i % 2
+            di = dev_in[sl]
+            with torch.cuda.stream(h2d_s):
+                h2d_s.wait_event(computed[sl])
+                for name in ("q", "k", "v"):
+                    di[name].copy_(host_in[name], non_blocking=True)
+                landed[sl].record(h2d_s)
+            stream.wait_event(landed[sl])
+            stream.wait_event(drained[sl])
+            a = b200attn.attention_forward(di["q"], di["k"], di["v"], pk, pv, ones, ones, pe,
+                                           out=attn, workspace=fwd_ws, status=status,
+                                           stream=stream).view(T, hl * HEAD_DIM)
+            if fused is not None and use_fused:
+                res = fused(a, w_out, h0, h1, status=status)
+            elif world == 1:
+                res = b200attn.gemm(a, w_cols, out=gemm_out[sl], status=status)
+            else:
+                res = step_nccl_tail(a)
+            res.record_stream(d2h_s)  # the copy-out stream still reads it
+            computed[sl].record(stream)
+            with torch.cuda.stream(d2h_s):
+                d2h_s.wait_event(computed[sl])
+                host_out[sl].copy_(res.view(T, hidden), non_blocking=True)
+                drained[sl].record(d2h_s)
+
+        for i in range(2):
+            e2e_step(i)
+        barrier()
+        n_e2e = max(args.e2e_steps, 2)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        h2d_s.wait_event(e0)
+        for i in range(n_e2e):
+            e2e_step(i)
+        stream.wait_event(drained[(n_e2e - 1) % 2])
+        e1.record(stream)
+        barrier()
+        e2e = dict(ms=e0.elapsed_time(e1) / n_e2e, h2d=3 * T * hl * HEAD_DIM * 2,
+                   d2h=T * hidden * 2)
     ms_fused = bdist.max_over_ranks(ms_fused, device=dev)
     ms_nccl = bdist.max_over_ranks(ms_nccl, device=dev)
+    e2e_ms = bdist.max_over_ranks(e2e["ms"], device=dev) if e2e else None
     ms_step = ms_fused if use_fused else ms_nccl
     attn_ms = bdist.max_over_ranks(attn_ms, device=dev)
     attn_flops = 4.0 * HEADS * T * (P + T) * HEAD_DIM
@@ -663,6 +727,11 @@ def run_head_sharded(args, cfg, rank, world, dev):
         pk_d, src = peaks()
         peak = float(pk_d.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
         achieved = attn_flops * hl / HEADS / (attn_ms / 1e3) / 1e12
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            value_c, _, _, threads_c, sample_c = c4_cpu_sample(args.cpu_heads, 1, 1)
+            cpu = {"value": value_c, "unit": "TFLOP/s", "cores": threads_c, "kind": "port",
+                   "sample": sample_c}
         line = {
             "metric": C4_METRIC,
             "value": (attn_flops + proj_flops) / (ms_step / 1e3) / 1e12, "unit": "TFLOP/s",
@@ -680,7 +749,14 @@ def run_head_sharded(args, cfg, rank, world, dev):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": None, "kernel": "joint_attn_kernel",
                          "peak_source": f"{src} bf16_tflops_sustained", "launch_ms": attn_ms},
-            "cpu_baseline": None, "e2e": None, "clocks": clocks.summary(),
+            "cpu_baseline": cpu, "clocks": clocks.summary(),
+            "e2e": None if e2e is None else {
+                "value": (attn_flops + proj_flops) / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                "ms_per_step": e2e_ms,
+                "path": ("b200_attn_fwd + to_out + sum of partials with this rank's pinned-host "
+                         "q/k/v in and the block output out; copies on their own streams, "
+                         "double-buffered")},
             "gpu_launches": args.steps * (4 if world > 1 and use_fused else 2 if world > 1 else 3),
         }
         print(json.dumps(line), flush=True)
