@@ -275,7 +275,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     n = static_cast<int>(static_cast<int64_t>(all) * (piece + 1) / p.split) - jb;
   }
 
+  // Producer (thread 0) helpers: Q, and key tile j of this unit into ring stage j % kStages
+  // (K, then V), completion counted on q_full / k_full / v_full.
+  auto load_q = [&]() {
+    mbar_expect_tx(q_full, kQTiles * kTileBytes);
+    for (int t = 0; t < kQTiles; ++t)
+      for (int c = 0; c < 2; ++c) {
+        uint8_t* dst = sQ + t * kTileBytes + c * kRegionBytes;
+        if (p.q_token_major)
+          tma_load_4d(dst, &tm_q, q_full, c * 64, h, q0 + t * kBM, b);
+        else
+          tma_load_4d(dst, &tm_q, q_full, c * 64, q0 + t * kBM, h, b);
+      }
+  };
+  auto load_k = [&](int j) {
+    const int s = j & 1;
+    const int ja = jb + j;  // tile index within the item
+    const bool seg0 = ja < n0;
+    const int row = (seg0 ? ja : ja - n0) * kBN;
+    mbar_expect_tx(k_full + s, kTileBytes);
+    for (int c = 0; c < 2; ++c) {
+      uint8_t* dst = sK + s * kTileBytes + c * kRegionBytes;
+      if (!seg0 && p.k1_token_major)
+        tma_load_4d(dst, &tm_k1, k_full + s, c * 64, h, row, b);
+      else
+        tma_load_4d(dst, seg0 ? &tm_k0 : &tm_k1, k_full + s, c * 64, row, h, b);
+    }
+  };
+  auto load_v = [&](int j) {
+    const int s = j & 1;
+    const int ja = jb + j;
+    const bool seg0 = ja < n0;
+    const int row = (seg0 ? ja : ja - n0) * kBN;
+    mbar_expect_tx(v_full + s, kTileBytes);
+    for (int c = 0; c < 2; ++c) {
+      uint8_t* dst = sV + s * kTileBytes + c * kRegionBytes;
+      if (seg0)
+        tma_load_4d(dst, &tm_v0, v_full + s, c * 64, row, h, b);
+      else if (p.v1_token_major)
+        tma_load_4d(dst, &tm_v1, v_full + s, c * 64, h, row, b);
+      else
+        tma_load_4d(dst, &tm_v1, v_full + s, c * 64, row, h, b);
+    }
+  };
   if (threadIdx.x == 0) {
+    if (n > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k1);
+      tma_prefetch_desc(&tm_v1);
+      if (n0 > 0) {
+        tma_prefetch_desc(&tm_k0);
+        tma_prefetch_desc(&tm_v0);
+      }
+    }
     mbar_init(q_full, 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(k_full + s, 1);
@@ -291,6 +343,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async();
+    // Q and the first kStages key tiles go out now: their latency overlaps the TMEM
+    // allocation and the CTA barrier below.
+    if (n > 0) {
+      load_q();
+      for (int j = 0; j < n && j < kStages; ++j) {
+        load_k(j);
+        load_v(j);
+      }
+    }
   }
   if (warp == 2) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -309,55 +370,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0 && n > 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k1);
-      tma_prefetch_desc(&tm_v1);
-      if (n0 > 0) {
-        tma_prefetch_desc(&tm_k0);
-        tma_prefetch_desc(&tm_v0);
-      }
-      mbar_expect_tx(q_full, kQTiles * kTileBytes);
-      for (int t = 0; t < kQTiles; ++t)
-        for (int c = 0; c < 2; ++c) {
-          uint8_t* dst = sQ + t * kTileBytes + c * kRegionBytes;
-          if (p.q_token_major)
-            tma_load_4d(dst, &tm_q, q_full, c * 64, h, q0 + t * kBM, b);
-          else
-            tma_load_4d(dst, &tm_q, q_full, c * 64, q0 + t * kBM, h, b);
-        }
+      // Q and key tiles [0, kStages) were issued before the CTA barrier.
       bool ok = true;
-      for (int j = 0; j < n && ok; ++j) {
+      for (int j = kStages; j < n && ok; ++j) {
         const int s = j & 1;
         const uint32_t u = static_cast<uint32_t>(j >> 1);
-        const int ja = jb + j;  // tile index within the item
-        const bool seg0 = ja < n0;
-        const int row = (seg0 ? ja : ja - n0) * kBN;
-        if (j >= kStages && !wait_or_abort(k_empty + s, (u - 1) & 1, abort_flag)) {
+        if (!wait_or_abort(k_empty + s, (u - 1) & 1, abort_flag)) {
           ok = false;
           break;
         }
-        mbar_expect_tx(k_full + s, kTileBytes);
-        for (int c = 0; c < 2; ++c) {
-          uint8_t* dst = sK + s * kTileBytes + c * kRegionBytes;
-          if (!seg0 && p.k1_token_major)
-            tma_load_4d(dst, &tm_k1, k_full + s, c * 64, h, row, b);
-          else
-            tma_load_4d(dst, seg0 ? &tm_k0 : &tm_k1, k_full + s, c * 64, row, h, b);
-        }
-        if (j >= kStages && !wait_or_abort(v_empty + s, (u - 1) & 1, abort_flag)) {
+        load_k(j);
+        if (!wait_or_abort(v_empty + s, (u - 1) & 1, abort_flag)) {
           ok = false;
           break;
         }
-        mbar_expect_tx(v_full + s, kTileBytes);
-        for (int c = 0; c < 2; ++c) {
-          uint8_t* dst = sV + s * kTileBytes + c * kRegionBytes;
-          if (seg0)
-            tma_load_4d(dst, &tm_v0, v_full + s, c * 64, row, h, b);
-          else if (p.v1_token_major)
-            tma_load_4d(dst, &tm_v1, v_full + s, c * 64, h, row, b);
-          else
-            tma_load_4d(dst, &tm_v1, v_full + s, c * 64, row, h, b);
-        }
+        load_v(j);
       }
       if (!ok) {
         record_error(p, abort_flag, 1);
