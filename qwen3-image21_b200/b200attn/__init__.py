@@ -4,6 +4,8 @@ without the built library on an sm_100 device the calls raise.
 
 Names mirror the reference's functions on this path:
   chunked_attention      src/transformer.rs:259  (q, k, v [B,H,S,D], scale, mask)
+  flash_attention        src/transformer.rs:243-254 (q, k, v [B,S,H,D], scale; the FA2
+                         branch, candle_flash_attn::flash_attn with causal = false)
   attention_forward      src/transformer.rs:179-193 (the norm -> RoPE -> cat -> attention
                          -> head-merge span of Attention::forward)
   joint_layout           src/joint_layout.rs:52  (JointLayout::new)
