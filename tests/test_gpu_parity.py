@@ -94,6 +94,18 @@ def test_norm_rope_matches_oracle(cuda):
     check(f32np(y), want, rel=3e-3)
 
 
+@pytest.mark.parametrize("B,T,H", [(1, 77, 40), (2, 33, 64), (1, 5, 33), (3, 17, 8)])
+def test_norm_rope_head_counts(cuda, B, T, H):
+    """Head counts past one warp's 32 rows per token (the kernel walks them 32 at a time)
+    and below it; ragged token counts."""
+    torch = _torch()
+    d, h = make_case(B, T, H, 0, 4200 + T + H, cuda)
+    y = b200attn.norm_rope(d["k"], d["wk"], 1e-6, d["pe"])
+    torch.cuda.synchronize()
+    want = ref.apply_rope(np.transpose(ref.rms_norm(h["k"], h["wk"]), (0, 2, 1, 3)), h["pe"])
+    assert np.max(np.abs(f32np(y) - want) / (np.abs(want) + 1e-3)) < 2 ** -8 + 1e-6
+
+
 # ------------------------------------------------------------------ plain attention
 @pytest.mark.parametrize("B,H,sq,skv", [
     (1, 1, 128, 128), (1, 2, 256, 256), (2, 3, 1, 1), (1, 2, 37, 300), (2, 1, 300, 129),
