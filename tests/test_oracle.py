@@ -100,6 +100,24 @@ def test_chunked_attention_matches_softmax(sq, skv):
     assert ref.rel_l2(got, want) < 1e-5
 
 
+def test_chunked_attention_matches_torch_sdpa():
+    """A third, independent implementation: torch's scaled_dot_product_attention (CPU,
+    float64) with the same boolean key mask."""
+    import torch
+    rng = np.random.default_rng(17)
+    q = rng.standard_normal((2, 3, 40, 128)).astype(np.float32)
+    k = rng.standard_normal((2, 3, 90, 128)).astype(np.float32)
+    v = rng.standard_normal((2, 3, 90, 128)).astype(np.float32)
+    mask = np.zeros((2, 1, 1, 90), bool)
+    mask[0, ..., :61] = True
+    mask[1, ..., :90] = True
+    got = ref.chunked_attention(q, k, v, 128 ** -0.5, mask)
+    t = lambda x: torch.from_numpy(x).double()
+    want = torch.nn.functional.scaled_dot_product_attention(
+        t(q), t(k), t(v), attn_mask=torch.from_numpy(mask), scale=128 ** -0.5).numpy()
+    assert ref.rel_l2(got, want) < 1e-5
+
+
 def test_chunked_attention_chunking_is_exact(monkeypatch):
     """The 256 MiB query chunk bounds memory only (src/transformer.rs:201-205): the result
     matches the unchunked one up to the GEMM's summation order."""
