@@ -15,6 +15,13 @@ Multi-GPU (torchrun, one process per GPU): independent generations, data-paralle
 collective on the data path (weak scaling); the barrier and a max-reduction of the
 timings use NCCL.  ``--impl reference`` times the CPU restatement of the reference's
 chunked attention (the reference is Rust/candle and cannot be built here) on the host.
+
+Other workloads (``--config``): c1 and c3 are the same step at 512^2 and for a 1024^2
+edit with a 10 624-token prefix; c4 is one head-sharded block at 2048^2 (attention of
+32/N heads per rank, its share of to_out, the cross-rank sum — fused over NVLink or NCCL —
+strong scaling); c5 is the 20-step denoising loop of 8 prompts x CFG (every block linear,
+the attention, the Euler update; Q4_K_M weights by default; ms per step, strong scaling).
+Each prints its own metric, and ``--impl reference`` prints the matching CPU arm.
 """
 from __future__ import annotations
 
