@@ -295,6 +295,7 @@ def _sampled_rows_check(out, h, rows):
 @pytest.mark.parametrize("T,P,pv", [
     (4096, 512, None),        # config 2 (1024^2 T2I)
     (4096, 10624, [10587]),   # config 3 (edit with two condition images, 37 padded keys)
+    (16384, 512, None),       # config 4 (2048^2, all 32 heads on one GPU: 132 key tiles)
 ])
 def test_full_size_configs(cuda, T, P, pv):
     torch = _torch()
