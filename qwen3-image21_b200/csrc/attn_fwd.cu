@@ -11,8 +11,12 @@
 //                      ring; S = Q K^T and O += P V run on tcgen05.mma (bf16 -> f32) with
 //                      S, P and O in tensor memory; two softmax warpgroups ping-pong so the
 //                      tensor core works on one Q tile while the other is in softmax.
-//                      Masking comes from per-batch key lengths.  Reference:
-//                      chunked_attention, src/transformer.rs:259-296.
+//                      Masking comes from per-batch key lengths (and, for the prefix
+//                      fill, per-row limits); the last partial wave of work items can be
+//                      cut by key range (tail split) and merged by the last piece.  Q, K
+//                      and V are read through 4-D tensor maps either head-major or
+//                      token-major.  Reference: chunked_attention,
+//                      src/transformer.rs:259-296; flash_attention, 243-254.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
