@@ -1,0 +1,30 @@
+"""The C ABI as a C caller sees it: every header in include/ compiles as C11 with warnings
+on, the program links against libb200attn.so, and the library's host-side entry points
+return the reference's known answers (tests/c_abi/c_abi_check.c; no GPU needed)."""
+import os
+import shutil
+import subprocess
+
+import pytest
+
+import b200attn
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_headers_compile_as_c_and_host_entry_points_answer(tmp_path):
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    b200attn.lib()  # builds nothing; raises if the library is missing
+    libdir = os.path.dirname(b200attn.LIB_PATH)
+    exe = tmp_path / "c_abi_check"
+    build = subprocess.run(
+        [cc, "-std=c11", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+         os.path.join(ROOT, "tests", "c_abi", "c_abi_check.c"), "-L", libdir, "-lb200attn",
+         f"-Wl,-rpath,{libdir}", "-lm", "-o", str(exe)],
+        capture_output=True, text=True)
+    assert build.returncode == 0, build.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stderr
+    assert "c abi ok" in run.stdout
