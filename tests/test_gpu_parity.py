@@ -170,6 +170,35 @@ def test_chunked_attention_key_mask(cuda):
         b200attn.chunked_attention(q.to(cuda), k.to(cuda), v.to(cuda), 128 ** -0.5, mask=bad.to(cuda))
 
 
+def test_no_valid_key_gives_nan_like_the_reference(cuda):
+    """A batch row whose key length is 0: the reference's softmax over an all -inf row is
+    NaN, and so is every output of that row; the other rows are unaffected.  Through both
+    the [B,H,S,D] and the [B,S,H,D] entry points."""
+    torch = _torch()
+    g = torch.Generator().manual_seed(23)
+    B, H, sq, skv = 3, 2, 70, 200
+    q = bf16(torch.randn(B, H, sq, 128, generator=g))
+    k = bf16(torch.randn(B, H, skv, 128, generator=g))
+    v = bf16(torch.randn(B, H, skv, 128, generator=g))
+    lens = [0, 57, 200]
+    key_len = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    out = b200attn.chunked_attention(q.to(cuda), k.to(cuda), v.to(cuda), 128 ** -0.5,
+                                     key_len=key_len)
+    t = lambda x: x.transpose(1, 2).contiguous().to(cuda)
+    out_fa = b200attn.flash_attention(t(q), t(k), t(v), 128 ** -0.5, key_len=key_len)
+    torch.cuda.synchronize()
+    mask = np.zeros((B, 1, 1, skv), bool)
+    for b, n in enumerate(lens):
+        mask[b, ..., :n] = True
+    with np.errstate(invalid="ignore"):
+        want = ref.chunked_attention(f32np(q), f32np(k), f32np(v), 128 ** -0.5, mask)
+    got = f32np(out)
+    got_fa = np.transpose(f32np(out_fa), (0, 2, 1, 3))
+    for arr in (got, got_fa):
+        assert np.isnan(arr[0]).all() and np.isnan(want[0]).all()
+        check(arr[1:], want[1:])
+
+
 def test_chunked_attention_scale_and_large_logits(cuda):
     """Logits far above 1 exercise the running-max rescale of O."""
     torch = _torch()
