@@ -754,7 +754,12 @@ def run_head_sharded(args, cfg, rank, world, dev):
                           "how": "cuBLAS to_out partial + NCCL all-reduce (bf16)"},
             "fused_path": {"ms_per_step": ms_fused, "how": fused_note},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None, "kernel": "joint_attn_kernel",
+                         "frac": achieved / peak,
+                         # captured with all 32 heads on one GPU; a rank's launch moves its
+                         # heads' share (traffic grows in proportion to the heads)
+                         "traffic": (None if profile_traffic("joint_attn_kernel", "c4") is None
+                                     else profile_traffic("joint_attn_kernel", "c4") * hl / HEADS),
+                         "kernel": "joint_attn_kernel",
                          "peak_source": f"{src} bf16_tflops_sustained", "launch_ms": attn_ms},
             "cpu_baseline": cpu, "clocks": clocks.summary(),
             "e2e": None if e2e is None else {
