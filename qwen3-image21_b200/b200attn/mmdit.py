@@ -169,6 +169,18 @@ class PrefixCache:
     v: List
     lengths: List[int]
 
+    def offload(self) -> "PrefixCache":
+        """set_kv_cache_offload (src/transformer.rs:27-45): keep the cache in pinned host
+        memory.  Cached steps then stream each layer's K and V back to the GPU on a copy
+        stream, one layer ahead of the attention that reads them."""
+        self.k = [t.cpu().pin_memory() for t in self.k]
+        self.v = [t.cpu().pin_memory() for t in self.v]
+        return self
+
+    @property
+    def on_host(self) -> bool:
+        return not self.k[0].is_cuda
+
 
 class MMDiT:
     """The transformer on one GPU with bf16 weights (see module docstring)."""
@@ -352,8 +364,41 @@ class MMDiT:
         ws_need = 2 * B * H * T * HEAD_DIM * 2 + b200attn.SPLIT_WORKSPACE_BYTES + 4096
         ws = self._buf("ws", (ws_need,), torch.uint8)
         b200attn.residual_adaln(x, None, None, scale1, y, rows_per_mod=R)      # norm1 of block 0
+        # A host-resident cache streams in one layer ahead: layer i's K/V land in staging
+        # slot i % 2 on the copy stream while layer i - 1 computes; a slot is refilled only
+        # after the attention that read it.
+        staged = None
+        if prefix is not None and prefix.on_host:
+            cur = torch.cuda.current_stream(self.device)
+            copy_stream = torch.cuda.Stream(self.device)
+            staged = [(torch.empty(prefix.k[0].shape, dtype=torch.bfloat16, device=self.device),
+                       torch.empty(prefix.v[0].shape, dtype=torch.bfloat16, device=self.device))
+                      for _ in range(2)]
+            landed = [torch.cuda.Event() for _ in range(2)]
+            consumed = [torch.cuda.Event() for _ in range(2)]
+
+            def stage(layer):
+                sl = layer % 2
+                if layer < 2:
+                    copy_stream.wait_stream(cur)  # the staging buffers were just allocated
+                else:
+                    copy_stream.wait_event(consumed[sl])  # layer - 2 has read this slot
+                with torch.cuda.stream(copy_stream):
+                    staged[sl][0].copy_(prefix.k[layer], non_blocking=True)
+                    staged[sl][1].copy_(prefix.v[layer], non_blocking=True)
+                    landed[sl].record(copy_stream)
+
+            stage(0)
         for i in range(len(self.blocks)):
             blk = self.block_weights(i)
+            pk = pv = None
+            if staged is not None:
+                if i + 1 < len(self.blocks):
+                    stage(i + 1)
+                cur.wait_event(landed[i % 2])
+                pk, pv = staged[i % 2]
+            elif prefix is not None:
+                pk, pv = prefix.k[i], prefix.v[i]
             fused = self.fused_qkv and kv_out is None and row_limit is None and H % 2 == 0
             if fused:   # projections + Q/K norm + RoPE in one GEMM, then the attention kernel
                 q_rot, k_rot, v = b200attn.qkv_norm_rope_gemm(
@@ -370,16 +415,16 @@ class MMDiT:
                 ev[0].record()
             if fused:
                 b200attn.joint_attention(
-                    q_rot, k_rot, v, None if prefix is None else prefix.k[i],
-                    None if prefix is None else prefix.v[i], desc=desc, out=attn,
+                    q_rot, k_rot, v, pk, pv, desc=desc, out=attn,
                     workspace=ws[:b200attn.SPLIT_WORKSPACE_BYTES])
             else:
                 b200attn.attention_forward(
-                    q, k, v, None if prefix is None else prefix.k[i],
-                    None if prefix is None else prefix.v[i], blk["nq"], blk["nk"], pe, desc=desc,
+                    q, k, v, pk, pv, blk["nq"], blk["nk"], pe, desc=desc,
                     out=attn, workspace=ws, row_limit=row_limit,
                     k_rot_out=None if kv_out is None else kv_out.k[i],
                     v_out=None if kv_out is None else kv_out.v[i])
+            if staged is not None:
+                consumed[i % 2].record(cur)
             if self.attn_marks is not None:
                 ev[1].record()
                 self.attn_marks.append(ev)
@@ -479,11 +524,12 @@ def cached_desc(cache: PrefixCache, target_len: int, device):
 
 
 def denoise(model: MMDiT, pos_embs: Sequence, neg_embs: Optional[Sequence], grid: Tuple[int, int],
-            steps: int, cfg_scale: float, noise, step_callback=None):
+            steps: int, cfg_scale: float, noise, step_callback=None, offload_cache: bool = False):
     """denoise (src/pipeline.rs:126-197) for a batch of prompts: noise f32 [n_prompts, T, C]
     (packed), one prefix cache for every positive and negative prompt, `steps` Euler steps
     with true CFG (neg + scale * (pos - neg)) when neg_embs is given.  Latents stay f32;
-    the transformer reads them as bf16.  Returns the final packed latents f32 [n, T, C]."""
+    the transformer reads them as bf16.  offload_cache keeps the prefix cache in pinned host
+    memory (set_kv_cache_offload).  Returns the final packed latents f32 [n, T, C]."""
     import torch
     n = noise.shape[0]
     T = grid[0] * grid[1]
@@ -491,6 +537,8 @@ def denoise(model: MMDiT, pos_embs: Sequence, neg_embs: Optional[Sequence], grid
     if neg_embs is not None:  # sequence order: p0 pos, p0 neg, p1 pos, p1 neg, ...
         embs = [e for pair in zip(pos_embs, neg_embs) for e in pair]
     cache = model.prefix_fill(embs)
+    if offload_cache:
+        cache.offload()
     pe = model.target_pe(cache.lengths, grid)
     desc = cached_desc(cache, T, model.device)
     sigmas = flow_match_sigmas(steps, T)

@@ -199,6 +199,28 @@ def test_cached_step_matches_oracle(tiny):
 
 
 @pytest.mark.gpu
+def test_host_offloaded_cache_gives_the_same_step(tiny):
+    """set_kv_cache_offload: with the prefix cache in pinned host memory, streamed back a
+    layer ahead of the attention, the cached step is bit-identical to the device cache's."""
+    _, model, _ = tiny
+    lengths = [33, 64]
+    embs = _embs(lengths, 8)
+    g = torch.Generator().manual_seed(12)
+    lat = torch.randn(len(lengths), 256, 64, generator=g).to("cuda:0")
+    cache = model.prefix_fill(embs)
+    pe = model.target_pe(lengths, GRID)
+    desc = mmdit.cached_desc(cache, 256, model.device)
+    on_device = model.step(lat, 0.4, cache, pe, desc).clone()
+    host = mmdit.PrefixCache(k=[t.clone() for t in cache.k], v=[t.clone() for t in cache.v],
+                             lengths=list(cache.lengths)).offload()
+    assert host.on_host and not cache.on_host
+    for _ in range(2):  # the staging slots are reused across calls
+        streamed = model.step(lat, 0.4, host, pe, desc)
+        torch.cuda.synchronize()
+        assert torch.equal(streamed, on_device)
+
+
+@pytest.mark.gpu
 def test_denoise_20_steps_with_cfg_matches_oracle(tiny):
     """End-to-end: 2 prompts x {pos, neg}, 20 FlowMatch Euler steps, true CFG 2.5 —
     final latents within rel L2 2e-2 of the float32 oracle.  (bf16 GEMM operands alone put
