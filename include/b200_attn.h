@@ -16,8 +16,12 @@
  *     the function says so.
  *   - Functions return 0 (B200_OK) or a negative b200_status; they never abort.
  *   - Tensors are dense row-major, bf16 unless stated.  head_dim must be 128.
- *   - Entry points are reentrant; the only process state is a per-device cache of
- *     kernel attributes guarded by a mutex.
+ *   - Entry points are reentrant, with one exception: b200_attn_fwd_noalloc, whose
+ *     calls share one scratch array per device (see there).  Process state: per-device
+ *     host caches (kernel attributes; the no-alloc array's device address), guarded by
+ *     mutexes and keyed by the CUDA context, so they are rebuilt after cudaDeviceReset;
+ *     and the no-alloc entry point's device array (B200_NOALLOC_SCRATCH_BYTES on every
+ *     GPU that loads this library's kernels).
  */
 #ifndef B200_ATTN_H
 #define B200_ATTN_H
@@ -134,10 +138,15 @@ int b200_attn_fwd(const b200_attn_args* args, b200_stream_t stream);
  * exceeds the limit return B200_ERR_WORKSPACE (e.g. with B = 1, H = 32: up to T = 4096
  * tokens with k_rot_out NULL, 8192 with it given); the tail split is used when its
  * region also fits.
- * The first call on a device looks up the array's device address (no allocation);
- * make that first call before any stream capture.  All calls on a device share the
- * one array: calls that may overlap on the GPU (other streams, other threads) race
- * on it, so serialise them.  Nothing in it needs clearing between calls.
+ * The first call on a device (and the first after the device's context changed, e.g.
+ * after cudaDeviceReset) looks up the array's device address (no allocation); make that
+ * first call before any stream capture.  The array's memory itself is committed when
+ * the CUDA module holding the library's kernels is loaded on the device: with lazy
+ * module loading (the CUDA 12 default) that is the first launch or symbol lookup of any
+ * of this library's attention entry points, so a caller that freezes its allocator
+ * should make one such call during warm-up, before the freeze.  All calls on a device
+ * share the one array: calls that may overlap on the GPU (other streams, other
+ * threads) race on it, so serialise them.  Nothing in it needs clearing between calls.
  */
 #define B200_NOALLOC_SCRATCH_BYTES (64u << 20)
 int b200_attn_fwd_noalloc(const b200_attn_args* args, b200_stream_t stream);

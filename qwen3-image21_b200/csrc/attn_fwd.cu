@@ -880,14 +880,47 @@ int make_map(CUtensorMap* map, const void* base, int B, int H, int rows, bool he
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_CUDA;
 }
 
+}  // namespace
+
+// Unique id of the calling thread's current CUDA context (cuCtxGetId: unique for the
+// life of the process, so a context re-created after cudaDeviceReset gets a new one);
+// 0 when there is no current context yet or the driver lacks the call.  Per-device host
+// caches of device state are keyed by it, so they are rebuilt after a reset.
+static unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+namespace {
+
 std::mutex g_attr_mutex;
-bool g_attr_done[64] = {};
+unsigned long long g_attr_ctx[64] = {};  // context the kernel attributes were set in
 
 int ensure_kernel_attrs() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return B200_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_attr_mutex);
-  if (dev >= 0 && dev < 64 && g_attr_done[dev]) return B200_OK;
+  const unsigned long long ctx = current_context_id();
+  if (dev >= 0 && dev < 64 && ctx != 0 && g_attr_ctx[dev] == ctx) return B200_OK;
   int major = 0, minor = 0;
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
@@ -895,7 +928,7 @@ int ensure_kernel_attrs() {
   if (cudaFuncSetAttribute(joint_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            kSmemBytes) != cudaSuccess)
     return B200_ERR_CUDA;
-  if (dev >= 0 && dev < 64) g_attr_done[dev] = true;
+  if (dev >= 0 && dev < 64) g_attr_ctx[dev] = current_context_id();
   return B200_OK;
 }
 
@@ -1224,7 +1257,8 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[B200_NOALLOC_SC
 
 namespace {
 std::mutex g_noalloc_mutex;
-void* g_noalloc_scratch_ptr[64] = {};  // device address of g_noalloc_scratch, per device
+void* g_noalloc_scratch_ptr[64] = {};             // device address of g_noalloc_scratch
+unsigned long long g_noalloc_scratch_ctx[64] = {};  // the context that address belongs to
 }  // namespace
 
 extern "C" int b200_attn_fwd_noalloc(const b200_attn_args* args, b200_stream_t stream) {
@@ -1243,12 +1277,16 @@ extern "C" int b200_attn_fwd_noalloc(const b200_attn_args* args, b200_stream_t s
   {
     // One-time set-up per device (with that device current): the host-side name of the
     // array is only a stand-in, so the kernels get its device address.
+    // The address is looked up again when the device's context changed (after a
+    // cudaDeviceReset the array lives at a new address in a new context).
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (!g_noalloc_scratch_ptr[dev]) {
+    const unsigned long long ctx = current_context_id();
+    if (!g_noalloc_scratch_ptr[dev] || ctx == 0 || g_noalloc_scratch_ctx[dev] != ctx) {
       void* ptr = nullptr;
       if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr)
         return B200_ERR_CUDA;
       g_noalloc_scratch_ptr[dev] = ptr;
+      g_noalloc_scratch_ctx[dev] = current_context_id();
     }
     scratch = g_noalloc_scratch_ptr[dev];
   }

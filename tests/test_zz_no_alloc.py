@@ -1,7 +1,8 @@
 """b200_attn_fwd_noalloc: the entry point for callers that cannot allocate device memory
 when they call (its scratch is a fixed array inside the library).  Checked through the C
-ABI against b200_attn_fwd with a caller workspace, on two calls in a row — the second
-call reuses the scratch the first one left behind, with a different shape and inputs.
+ABI against b200_attn_fwd with a caller workspace and against the CPU oracle, on two
+calls in a row — the second call reuses the scratch the first one left behind, with a
+different shape and inputs.
 
 This file is collected last so that a run stopping at the first failure has already run
 every other test; it also passes alone in a fresh process."""
@@ -11,6 +12,7 @@ import numpy as np
 import pytest
 
 import b200attn
+from oracle import cpu as ocpu
 from oracle import reference as ref
 
 pytestmark = pytest.mark.gpu
@@ -71,6 +73,14 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda):
         assert np.isfinite(got).all()
         assert ref.rel_l2(got, ref_out) <= REL_L2
         assert float(np.max(np.abs(got - ref_out))) <= MAX_ABS
+        # and directly against the CPU oracle (the f32 restatement of the reference span)
+        bits = lambda t: t.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+        oracle_out = ocpu.attention_forward(
+            bits(d["q"]), bits(d["k"]), bits(d["v"]), bits(d["pk"]), bits(d["pv"]),
+            d["wq"].cpu().numpy(), d["wk"].cpu().numpy(), 1e-6, d["pe"].cpu().numpy(),
+            np.array(pv, np.int32), 128 ** -0.5)
+        assert ref.rel_l2(got, oracle_out) <= REL_L2
+        assert float(np.max(np.abs(got - oracle_out))) <= MAX_ABS
         if with_k:
             want_k = b200attn.norm_rope(d["k"], d["wk"], 1e-6, d["pe"])
             torch.cuda.synchronize()
