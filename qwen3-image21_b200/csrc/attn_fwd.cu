@@ -160,13 +160,13 @@ constexpr int kPolyEvery = 4;
 // thread): keys >= valid are masked (kMasked); the running max m (log2 units) is raised
 // only when the row max exceeds it by more than kRescaleThreshold (lazy rescaling, as in
 // FlashAttention-4), so P = 2^(S*c - m) <= 2^8.  P goes to TMEM columns [tS, tS + 64) as
-// bf16 pairs, over S columns already read.  Updates the running sum l and returns the
-// factor the O accumulator must be scaled by (1 when m did not move).  A row without any
-// valid key so far keeps m = -inf, P = 0 and l = 0.
+// bf16 pairs, over S columns already read; the f32 p values stay in r for the row sum,
+// which the caller takes after handing P to the MMA warp (off the S -> P critical path).
+// Returns the factor the O accumulator must be scaled by (1 when m did not move).  A row
+// without any valid key so far keeps m = -inf and P = 0.
 template <bool kMasked>
-__device__ __forceinline__ float softmax_row(const int valid, const float c, float& m, float& l,
-                                             const uint32_t tS) {
-  uint32_t r[4][32];
+__device__ __forceinline__ float softmax_row(uint32_t (&r)[4][32], const int valid,
+                                             const float c, float& m, const uint32_t tS) {
 #pragma unroll
   for (int q = 0; q < 4; ++q) tmem_ld32(tS + q * 32, r[q]);
   tmem_wait_ld();
@@ -197,7 +197,6 @@ __device__ __forceinline__ float softmax_row(const int valid, const float c, flo
   // P = 2^-inf = 0, not 2^(-inf + inf) = NaN (a tail-split piece can hold such rows).
   const float m_ref = m == -INFINITY ? 0.f : m;
   const uint64_t nm = f2pack(-m_ref, -m_ref);
-  uint64_t acc[4] = {f2pack(0.f, 0.f), f2pack(0.f, 0.f), f2pack(0.f, 0.f), f2pack(0.f, 0.f)};
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     uint32_t pk[32];
@@ -212,16 +211,26 @@ __device__ __forceinline__ float softmax_row(const int valid, const float c, flo
         p0 = ex2_approx(x0);
         p1 = ex2_approx(x1);
       }
-      acc[i & 3] = f2add(acc[i & 3], f2pack(p0, p1));
+      r[col >> 5][col & 31] = __float_as_uint(p0);
+      r[(col + 1) >> 5][(col + 1) & 31] = __float_as_uint(p1);
       pk[i] = pack_bf16x2(p0, p1);
     }
     tmem_st32(tS + half * 32, pk);
   }
+  return alpha;
+}
+
+// Sum of the 128 f32 p values softmax_row left in r (4 independent f32x2 chains).
+__device__ __forceinline__ float row_sum(const uint32_t (&r)[4][32]) {
+  uint64_t acc[4] = {f2pack(0.f, 0.f), f2pack(0.f, 0.f), f2pack(0.f, 0.f), f2pack(0.f, 0.f)};
+#pragma unroll
+  for (int i = 0; i < 64; ++i)
+    acc[i & 3] = f2add(acc[i & 3], f2pack(__uint_as_float(r[(2 * i) >> 5][(2 * i) & 31]),
+                                          __uint_as_float(r[(2 * i + 1) >> 5][(2 * i + 1) & 31])));
   float s[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) f2unpack(acc[i], s[2 * i], s[2 * i + 1]);
-  l = l * alpha + (((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7])));
-  return alpha;
+  return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -401,7 +410,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0 && n > 0) {
+    // The whole warp runs the loop (every lane waits; the lanes agree through __all_sync),
+    // and one elected lane issues each tcgen05.mma / commit (always the same lane, so its
+    // commits track its own MMAs).
+    if (n > 0) {
       constexpr uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = idesc_bf16_f32(kBM, kD, 0, 1);
       // Descriptors as (low, high) words: a k-step only moves the start address (low 14
@@ -414,42 +426,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t hi_v = static_cast<uint32_t>(dV >> 32);
       const uint32_t lo_q = static_cast<uint32_t>(dQ), lo_k = static_cast<uint32_t>(dK);
       const uint32_t lo_v = static_cast<uint32_t>(dV);
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, wait_or_abort(bar, parity, abort_flag));
+      };
+      auto commit = [&](uint64_t* bar) {
+        if (elect_one()) mma_commit(bar);
+      };
       auto qk = [&](int t, int s) {
         const uint32_t d = tmem_base + t * kBN;
         const uint32_t a = lo_q + ((t * kTileBytes) >> 4);
         const uint32_t bk = lo_k + ((s * kTileBytes) >> 4);
         // k-step kk: region kk/4 (16 KiB apart), 32 bytes per step inside the swizzle span
-        mma_ss_off<0, 0>(d, a, hi_qk, bk, hi_qk, idesc_qk, 0u);
-        mma_ss_off<2, 2>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
-        mma_ss_off<4, 4>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
-        mma_ss_off<6, 6>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
-        mma_ss_off<1024, 1024>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
-        mma_ss_off<1026, 1026>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
-        mma_ss_off<1028, 1028>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
-        mma_ss_off<1030, 1030>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+        if (elect_one()) {
+          mma_ss_off<0, 0>(d, a, hi_qk, bk, hi_qk, idesc_qk, 0u);
+          mma_ss_off<2, 2>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+          mma_ss_off<4, 4>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+          mma_ss_off<6, 6>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+          mma_ss_off<1024, 1024>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+          mma_ss_off<1026, 1026>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+          mma_ss_off<1028, 1028>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+          mma_ss_off<1030, 1030>(d, a, hi_qk, bk, hi_qk, idesc_qk, 1u);
+        }
+        __syncwarp();
       };
       auto pv_mma = [&](int t, int s, bool acc) {
         const uint32_t d = tmem_base + 2 * kBN + t * kD;
         const uint32_t a = tmem_base + t * kBN;  // P (bf16 pairs) over S's first 64 columns
         const uint32_t bv = lo_v + ((s * kTileBytes) >> 4);
         // k-step kk: 16 keys = 2 KiB of V rows; P columns kk*8 .. kk*8+7
-        mma_ts_off<0>(d, a, bv, hi_v, idesc_pv, acc ? 1u : 0u);
-        mma_ts_off<128>(d, a + 8, bv, hi_v, idesc_pv, 1u);
-        mma_ts_off<256>(d, a + 16, bv, hi_v, idesc_pv, 1u);
-        mma_ts_off<384>(d, a + 24, bv, hi_v, idesc_pv, 1u);
-        mma_ts_off<512>(d, a + 32, bv, hi_v, idesc_pv, 1u);
-        mma_ts_off<640>(d, a + 40, bv, hi_v, idesc_pv, 1u);
-        mma_ts_off<768>(d, a + 48, bv, hi_v, idesc_pv, 1u);
-        mma_ts_off<896>(d, a + 56, bv, hi_v, idesc_pv, 1u);
+        if (elect_one()) {
+          mma_ts_off<0>(d, a, bv, hi_v, idesc_pv, acc ? 1u : 0u);
+          mma_ts_off<128>(d, a + 8, bv, hi_v, idesc_pv, 1u);
+          mma_ts_off<256>(d, a + 16, bv, hi_v, idesc_pv, 1u);
+          mma_ts_off<384>(d, a + 24, bv, hi_v, idesc_pv, 1u);
+          mma_ts_off<512>(d, a + 32, bv, hi_v, idesc_pv, 1u);
+          mma_ts_off<640>(d, a + 40, bv, hi_v, idesc_pv, 1u);
+          mma_ts_off<768>(d, a + 48, bv, hi_v, idesc_pv, 1u);
+          mma_ts_off<896>(d, a + 56, bv, hi_v, idesc_pv, 1u);
+        }
+        __syncwarp();
       };
-      bool ok = wait_or_abort(q_full, 0, abort_flag) && wait_or_abort(k_full, 0, abort_flag);
+      bool ok = wait(q_full, 0) && wait(k_full, 0);
       if (ok) {
         tc_fence_after();
         qk(0, 0);
-        mma_commit(s_full + 0);
+        commit(s_full + 0);
         qk(1, 0);
-        mma_commit(s_full + 1);
-        mma_commit(k_empty + 0);
+        commit(s_full + 1);
+        commit(k_empty + 0);
       }
       for (int j = 0; j < n && ok; ++j) {
         const int s = j & 1;
@@ -457,38 +481,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s1 = (j + 1) & 1;
         const uint32_t u1 = static_cast<uint32_t>((j + 1) >> 1);
         const bool more = j + 1 < n;
-        if (!wait_or_abort(v_full + s, u & 1, abort_flag) ||
-            !wait_or_abort(p_full + 0, j & 1, abort_flag)) {
+        if (!wait(v_full + s, u & 1) || !wait(p_full + 0, j & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
         pv_mma(0, s, j > 0);
-        if (!more) mma_commit(o_full + 0);
+        if (!more) commit(o_full + 0);
         if (more) {
-          if (!wait_or_abort(k_full + s1, u1 & 1, abort_flag)) {
+          if (!wait(k_full + s1, u1 & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
           qk(0, s1);
-          mma_commit(s_full + 0);
+          commit(s_full + 0);
         }
-        if (!wait_or_abort(p_full + 1, j & 1, abort_flag)) {
+        if (!wait(p_full + 1, j & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
         pv_mma(1, s, j > 0);
-        mma_commit(v_empty + s);
-        if (!more) mma_commit(o_full + 1);
+        commit(v_empty + s);
+        if (!more) commit(o_full + 1);
         if (more) {
           qk(1, s1);
-          mma_commit(s_full + 1);
-          mma_commit(k_empty + s1);
+          commit(s_full + 1);
+          commit(k_empty + s1);
         }
       }
-      if (!ok) record_error(p, abort_flag, 2);
+      if (!ok && lane == 0) record_error(p, abort_flag, 2);
     }
   }
   } else {
@@ -518,9 +541,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int valid = ja < n0 ? min(kBN, pv - ja * kBN) : min(kBN, tv_row - (ja - n0) * kBN);
       // Rows of a warp may have different limits: any masked lane sends the whole warp down
       // the masked path (TMEM loads are warp-collective).
+      uint32_t r[4][32];
       const float alpha = __any_sync(0xffffffffu, valid < kBN)
-                              ? softmax_row<true>(valid, c, m, l, tS)
-                              : softmax_row<false>(valid, c, m, l, tS);
+                              ? softmax_row<true>(r, valid, c, m, tS)
+                              : softmax_row<false>(r, valid, c, m, tS);
       // O rescale: PV of the previous tile is complete (s_full is committed after it).
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
@@ -536,6 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_full + t);
+      l = l * alpha + row_sum(r);
     }
     if (!ok) record_error(p, abort_flag, 3);
     // Epilogue: O / l -> bf16 rows of `out`.

@@ -181,6 +181,21 @@ __device__ __forceinline__ void mma_ts_off(uint32_t d_tmem, uint32_t a_tmem, uin
       : "memory");
 }
 
+// One lane of a converged warp (the lowest active one, the same lane on every call with
+// the full mask).  Issuing tcgen05.mma from a converged warp through an elected lane lets
+// the compiler keep the warp-uniform descriptors in uniform registers; issuing from a
+// divergent single-thread branch costs register moves per instruction, and at N = 128
+// that made the issue slower than the tensor pipe.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Arrive once on `bar` when every tcgen05 operation this thread issued so far is done.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
