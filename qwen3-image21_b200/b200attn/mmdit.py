@@ -262,6 +262,19 @@ class MMDiT:
             self._bufs[name] = t
         return t[:n].view(*shape)
 
+    def _copy_stream(self):
+        """The model's host<->device copy stream (created once)."""
+        import torch
+        if getattr(self, "_copy", None) is None:
+            self._copy = torch.cuda.Stream(self.device)
+        return self._copy
+
+    def _staging(self, tag: str, shape):
+        """Two (K, V) device staging slots of `shape` bf16, kept across calls."""
+        import torch
+        return [(self._buf(f"stage_{tag}_k{j}", tuple(shape), torch.bfloat16),
+                 self._buf(f"stage_{tag}_v{j}", tuple(shape), torch.bfloat16)) for j in range(2)]
+
     def time_embed(self, t: float):
         """QwenTimestepProj (src/transformer.rs:112-114) of timestep_embedding(t) -> f32 [hidden]."""
         import torch
@@ -368,19 +381,17 @@ class MMDiT:
         # slot i % 2 on the copy stream while layer i - 1 computes; a slot is refilled only
         # after the attention that read it.
         staged = None
+        cur = torch.cuda.current_stream(self.device)
         if prefix is not None and prefix.on_host:
-            cur = torch.cuda.current_stream(self.device)
-            copy_stream = torch.cuda.Stream(self.device)
-            staged = [(torch.empty(prefix.k[0].shape, dtype=torch.bfloat16, device=self.device),
-                       torch.empty(prefix.v[0].shape, dtype=torch.bfloat16, device=self.device))
-                      for _ in range(2)]
+            copy_stream = self._copy_stream()
+            staged = self._staging("in", prefix.k[0].shape)
             landed = [torch.cuda.Event() for _ in range(2)]
             consumed = [torch.cuda.Event() for _ in range(2)]
 
             def stage(layer):
                 sl = layer % 2
                 if layer < 2:
-                    copy_stream.wait_stream(cur)  # the staging buffers were just allocated
+                    copy_stream.wait_stream(cur)  # earlier work on the slots is ordered first
                 else:
                     copy_stream.wait_event(consumed[sl])  # layer - 2 has read this slot
                 with torch.cuda.stream(copy_stream):
@@ -389,6 +400,15 @@ class MMDiT:
                     landed[sl].record(copy_stream)
 
             stage(0)
+        # A host-resident prefix pass (prefix_fill(offload=True)) writes each layer's K/V
+        # into device staging slot i % 2 and drains it to the pinned host cache on the copy
+        # stream while the next layer computes; a slot is rewritten only after its drain.
+        sink = None
+        if kv_out is not None and kv_out.on_host:
+            sink_stream = self._copy_stream()
+            sink = self._staging("out", kv_out.k[0].shape)
+            computed = [torch.cuda.Event() for _ in range(2)]
+            drained = [None, None]
         for i in range(len(self.blocks)):
             blk = self.block_weights(i)
             pk = pv = None
@@ -418,11 +438,25 @@ class MMDiT:
                     q_rot, k_rot, v, pk, pv, desc=desc, out=attn,
                     workspace=ws[:b200attn.SPLIT_WORKSPACE_BYTES])
             else:
+                k_dst = v_dst = None
+                if sink is not None:
+                    if drained[i % 2] is not None:
+                        cur.wait_event(drained[i % 2])  # layer i - 2 has left this slot
+                    k_dst, v_dst = sink[i % 2]
+                elif kv_out is not None:
+                    k_dst, v_dst = kv_out.k[i], kv_out.v[i]
                 b200attn.attention_forward(
                     q, k, v, pk, pv, blk["nq"], blk["nk"], pe, desc=desc,
-                    out=attn, workspace=ws, row_limit=row_limit,
-                    k_rot_out=None if kv_out is None else kv_out.k[i],
-                    v_out=None if kv_out is None else kv_out.v[i])
+                    out=attn, workspace=ws, row_limit=row_limit, k_rot_out=k_dst, v_out=v_dst)
+                if sink is not None:
+                    sl = i % 2
+                    computed[sl].record(cur)
+                    sink_stream.wait_event(computed[sl])
+                    with torch.cuda.stream(sink_stream):
+                        kv_out.k[i].copy_(k_dst, non_blocking=True)
+                        kv_out.v[i].copy_(v_dst, non_blocking=True)
+                        drained[sl] = torch.cuda.Event()
+                        drained[sl].record(sink_stream)
             if staged is not None:
                 consumed[i % 2].record(cur)
             if self.attn_marks is not None:
@@ -437,6 +471,10 @@ class MMDiT:
                 hh = b200attn.swiglu(gp, self._buf("h", (r1 - r0, cfg.ffn), torch.bfloat16))
                 self._gemm(hh, blk["wmo"], "mo", out=mo[r0:r1])
             last = i + 1 == len(self.blocks)
+            if last and sink is not None:
+                for ev in drained:  # the host cache is complete when the pass is
+                    if ev is not None:
+                        cur.wait_event(ev)
             if not last:
                 b200attn.residual_adaln(x, mo, gate2, scale1, y, rows_per_mod=R)  # next norm1
             elif final_scale is not None:
@@ -457,12 +495,18 @@ class MMDiT:
         a = F.gelu((e.to(torch.bfloat16) @ self.txt_in1.t()).float(), approximate="tanh")
         return (a.to(torch.bfloat16) @ self.txt_in2.t()).float()
 
-    def prefix_fill(self, text_embs: Sequence) -> PrefixCache:
+    def prefix_fill(self, text_embs: Sequence, offload: bool = False) -> PrefixCache:
         """prefix_kv (src/transformer.rs:674-707) for a batch of text-only prompts of ragged
         lengths, in one pass: the prompts are padded to Pmax rows, each row's descriptor
         limits its keys to its own length, and the text rows' causal mask
         (build_block_causal_mask over image_ids = -1) is the row-limit list 1..Pmax.  The
-        attention writes post-RoPE K and V straight into the cache layout."""
+        attention writes post-RoPE K and V straight into the cache layout.
+
+        offload=True (set_kv_cache_offload, src/transformer.rs:27-45, which moves each
+        layer's entry to the CPU as it is computed): the cache is allocated in pinned host
+        memory up front and each layer's K/V goes through one of two reused device staging
+        slots, drained to the host on a copy stream while the next layer computes, so the
+        device never holds more than two layers of it."""
         import torch
         cfg = self.cfg
         B = len(text_embs)
@@ -472,12 +516,13 @@ class MMDiT:
         for b, e in enumerate(text_embs):
             emb[b, :lengths[b]] = e.to(self.device, torch.bfloat16)
         x = self.text_embed(emb.view(B * P, cfg.text_dim)).contiguous()
-        cache = PrefixCache(
-            k=[torch.zeros((B, cfg.heads, P, HEAD_DIM), dtype=torch.bfloat16, device=self.device)
-               for _ in range(cfg.layers)],
-            v=[torch.zeros((B, cfg.heads, P, HEAD_DIM), dtype=torch.bfloat16, device=self.device)
-               for _ in range(cfg.layers)],
-            lengths=lengths)
+        shape = (B, cfg.heads, P, HEAD_DIM)
+        if offload:
+            alloc = lambda: torch.empty(shape, dtype=torch.bfloat16).pin_memory()
+        else:
+            alloc = lambda: torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
+        cache = PrefixCache(k=[alloc() for _ in range(cfg.layers)],
+                            v=[alloc() for _ in range(cfg.layers)], lengths=lengths)
         lay = b200attn.joint_layout(P, None, [], (0, 0))
         pe = torch.from_numpy(b200attn.rope_pe(lay["img_shapes"], lay["image_pad_mask"], AXES,
                                                ROPE_THETA)[:P]).to(self.device)
@@ -536,9 +581,7 @@ def denoise(model: MMDiT, pos_embs: Sequence, neg_embs: Optional[Sequence], grid
     embs = list(pos_embs)
     if neg_embs is not None:  # sequence order: p0 pos, p0 neg, p1 pos, p1 neg, ...
         embs = [e for pair in zip(pos_embs, neg_embs) for e in pair]
-    cache = model.prefix_fill(embs)
-    if offload_cache:
-        cache.offload()
+    cache = model.prefix_fill(embs, offload=offload_cache)
     pe = model.target_pe(cache.lengths, grid)
     desc = cached_desc(cache, T, model.device)
     sigmas = flow_match_sigmas(steps, T)

@@ -214,10 +214,56 @@ def test_host_offloaded_cache_gives_the_same_step(tiny):
     host = mmdit.PrefixCache(k=[t.clone() for t in cache.k], v=[t.clone() for t in cache.v],
                              lengths=list(cache.lengths)).offload()
     assert host.on_host and not cache.on_host
-    for _ in range(2):  # the staging slots are reused across calls
+    slots = None
+    for _ in range(2):  # the model's staging slots are reused across calls
         streamed = model.step(lat, 0.4, host, pe, desc)
         torch.cuda.synchronize()
         assert torch.equal(streamed, on_device)
+        now = [t.data_ptr() for pair in model._staging("in", host.k[0].shape) for t in pair]
+        assert slots is None or now == slots
+        slots = now
+
+
+@pytest.mark.gpu
+def test_prefix_fill_offload_streams_each_layer_to_host():
+    """prefix_fill(offload=True): each layer's K/V leaves the GPU as it is computed (two
+    device staging slots), so the fill's peak device memory grows by a small part of the
+    cache instead of the whole cache; the host cache equals the device-filled one bit for
+    bit, and the offloaded fill then drives the same cached step."""
+    cfg = mmdit.MMDiTConfig(layers=16, heads=2, text_dim=256)
+    model = mmdit.MMDiT(cfg, mmdit.random_weights(cfg, 3, std=STD), device="cuda:0")
+    lengths = [1500, 1100]
+    embs = _embs(lengths, 21)
+    dev_cache = model.prefix_fill(embs)          # also sizes the model's work buffers
+    torch.cuda.synchronize()
+    cache_bytes = sum(t.numel() * 2 for t in dev_cache.k + dev_cache.v)
+
+    def peak_growth(fn):
+        torch.cuda.synchronize()
+        base = torch.cuda.memory_allocated()
+        torch.cuda.reset_peak_memory_stats()
+        out = fn()
+        torch.cuda.synchronize()
+        return out, torch.cuda.max_memory_allocated() - base
+
+    again, grow_dev = peak_growth(lambda: model.prefix_fill(embs))
+    host = model.prefix_fill(embs, offload=True)   # sizes the two staging slots
+    host_again, grow_off = peak_growth(lambda: model.prefix_fill(embs, offload=True))
+    assert host.on_host and all(t.is_pinned() for t in host.k + host.v)
+    assert grow_dev >= cache_bytes
+    assert grow_off <= cache_bytes // 4, (grow_off, cache_bytes)
+    for i in range(cfg.layers):
+        assert torch.equal(host.k[i], dev_cache.k[i].cpu()) and torch.equal(host.v[i], dev_cache.v[i].cpu())
+        assert torch.equal(host_again.k[i], host.k[i])   # staging slots reused across fills
+    del again
+    g = torch.Generator().manual_seed(22)
+    lat = torch.randn(len(lengths), 256, 64, generator=g).to("cuda:0")
+    pe = model.target_pe(lengths, GRID)
+    desc = mmdit.cached_desc(dev_cache, 256, model.device)
+    want = model.step(lat, 0.3, dev_cache, pe, desc).clone()
+    got = model.step(lat, 0.3, host, pe, desc)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
 
 
 @pytest.mark.gpu
