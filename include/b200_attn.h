@@ -34,7 +34,7 @@ extern "C" {
 #endif
 
 #define B200_ATTN_HEAD_DIM 128
-#define B200_ATTN_ABI_VERSION 3
+#define B200_ATTN_ABI_VERSION 4
 
 typedef enum {
   B200_OK = 0,
@@ -45,6 +45,10 @@ typedef enum {
   B200_ERR_LAYOUT = -5,      /* layout / mask not representable (see key_valid)     */
   B200_ERR_DEVICE_TIMEOUT = -6 /* a device-side wait ran out (status word)          */
 } b200_status;
+
+/* Element types named by entry points that take more than one (b200_flash_attention_ex,
+ * the head-sharding communicator of b200_tp.h). */
+typedef enum { B200_DTYPE_BF16 = 0, B200_DTYPE_F32 = 1, B200_DTYPE_F16 = 2 } b200_dtype;
 
 /* Opaque CUDA stream (cudaStream_t / CUstream); NULL = legacy default stream. */
 typedef void* b200_stream_t;
@@ -170,16 +174,26 @@ int b200_joint_attention(const void* q_rot, const void* k_rot, const void* v,
 
 /*
  * The FA2 branch's contract on [B,S,H,D] tensors: out = softmax(q k^T * scale [masked]) v
- * with token-major q [B,Sq,H,D], k, v [B,Skv,H,D] and out [B,Sq,H,D] (all bf16), no
- * transposes.  Replaces flash_attention / candle_flash_attn::flash_attn(q, k, v, scale,
- * causal = false) (src/transformer.rs:243-254), whose tensors have this layout.  key_len
- * (device int32 [B] or NULL): batch row b attends to keys [0, key_len[b]).  One kernel on
- * `stream`; no workspace, no host sync.
+ * with token-major q [B,Sq,H,D], k, v [B,Skv,H,D] and out [B,Sq,H,D], no transposes.
+ * Replaces flash_attention / candle_flash_attn::flash_attn(q, k, v, scale, causal = false)
+ * (src/transformer.rs:243-254), whose tensors have this layout.  key_len (device int32 [B]
+ * or NULL): batch row b attends to keys [0, key_len[b]).  One kernel on `stream`; no
+ * workspace, no host sync.
+ *
+ * b200_flash_attention takes bf16 tensors.  b200_flash_attention_ex takes the element
+ * type: B200_DTYPE_BF16, or B200_DTYPE_F16 for IEEE half q/k/v/out, the type the
+ * reference's FA2 branch casts its inputs to (src/transformer.rs:244-251).  Any other
+ * dtype returns B200_ERR_UNSUPPORTED before launching.  Both compute in f32 (scores,
+ * softmax, accumulation) with P rounded to the input type for the P.V product.
  */
 int b200_flash_attention(const void* q, const void* k, const void* v, void* out,
                          int32_t batch, int32_t sq, int32_t skv, int32_t heads,
                          int32_t head_dim, float scale, const int32_t* key_len,
                          int32_t* status, b200_stream_t stream);
+int b200_flash_attention_ex(const void* q, const void* k, const void* v, void* out,
+                            int32_t batch, int32_t sq, int32_t skv, int32_t heads,
+                            int32_t head_dim, float scale, const int32_t* key_len,
+                            int32_t dtype, int32_t* status, b200_stream_t stream);
 
 /*
  * Plain attention on [B,H,S,D] tensors: out = softmax(q k^T * scale [masked]) v.

@@ -33,7 +33,7 @@ extern "C" {
 
 typedef struct b200_tp_comm b200_tp_comm; /* opaque */
 
-typedef enum { B200_DTYPE_BF16 = 0, B200_DTYPE_F32 = 1 } b200_dtype;
+/* b200_dtype (B200_DTYPE_BF16 / B200_DTYPE_F32 here) is declared in b200_attn.h. */
 
 /* A new group id, made on one rank and handed to every rank by the caller (store, MPI,
  * file ...).  B200_ERR_UNSUPPORTED when NCCL cannot be loaded. */

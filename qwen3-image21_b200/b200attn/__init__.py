@@ -30,7 +30,7 @@ OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE, ERR_LAYOUT, ERR_DEVIC
 
 EXPORTED = (
     "b200_attn_workspace_bytes", "b200_attn_fwd", "b200_joint_attention", "b200_chunked_attention",
-    "b200_flash_attention",
+    "b200_flash_attention", "b200_flash_attention_ex",
     "b200_norm_rope", "b200_qk_norm_rope",
     "b200_joint_layout", "b200_rope_positions", "b200_rope_pe", "b200_key_valid_to_desc",
     "b200_block_causal_limits",
@@ -85,6 +85,8 @@ def lib() -> ctypes.CDLL:
         L.b200_attn_fwd.argtypes = [ctypes.POINTER(AttnArgs), vp]
         L.b200_chunked_attention.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, vp, vp, vp]
         L.b200_flash_attention.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, vp, vp, vp]
+        L.b200_flash_attention_ex.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, vp, i32,
+                                              vp, vp]
         L.b200_norm_rope.argtypes = [vp, vp, i32, i32, i32, i32, vp, f32, vp, vp]
         L.b200_qk_norm_rope.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, vp, vp, f32, vp, vp]
         L.b200_joint_attention.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, f32, vp,
@@ -266,17 +268,21 @@ def attention_forward(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w, pe, desc=
 
 
 def flash_attention(q, k, v, scale: float, key_len=None, status=None, out=None, stream=None):
-    """flash_attention / flash_attn(q, k, v, scale, causal=False) on [B,S,H,D] bf16 tensors
-    (token-major, no transposes) -> out [B,Sq,H,D].  ``key_len`` (int32 device tensor [B]):
-    batch row b attends to keys [0, key_len[b])."""
+    """flash_attention / flash_attn(q, k, v, scale, causal=False) on [B,S,H,D] tensors
+    (token-major, no transposes) -> out [B,Sq,H,D] of the same type.  bf16 or float16 (the
+    type the reference's FA2 branch casts to); any other dtype raises B200Error
+    ERR_UNSUPPORTED from the library.  ``key_len`` (int32 device tensor [B]): batch row b
+    attends to keys [0, key_len[b])."""
     import torch
     b, sq, h, d = q.shape
     skv = k.shape[1]
+    dtype = {torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}.get(q.dtype, -1)
     if out is None:
-        out = torch.empty((b, sq, h, d), dtype=torch.bfloat16, device=q.device)
-    _check(lib().b200_flash_attention(_dptr(q), _dptr(k), _dptr(v), _dptr(out), b, sq, skv, h, d,
-                                      float(scale), _dptr(key_len), _dptr(status), _stream(stream)),
-           "b200_flash_attention")
+        out = torch.empty((b, sq, h, d), dtype=q.dtype, device=q.device)
+    _check(lib().b200_flash_attention_ex(_dptr(q), _dptr(k), _dptr(v), _dptr(out), b, sq, skv, h,
+                                         d, float(scale), _dptr(key_len), dtype, _dptr(status),
+                                         _stream(stream)),
+           "b200_flash_attention_ex")
     return out
 
 
@@ -488,7 +494,7 @@ def qkv_norm_rope_gemm(x, w_qkv, batch: int, tokens: int, heads: int, norm_q_w, 
 
 # ----------------------------------------------------------------- head-sharding communicator
 TP_ID_BYTES = 128  # B200_TP_ID_BYTES
-DTYPE_BF16, DTYPE_F32 = 0, 1
+DTYPE_BF16, DTYPE_F32, DTYPE_F16 = 0, 1, 2  # b200_dtype
 
 
 def tp_unique_id() -> bytes:

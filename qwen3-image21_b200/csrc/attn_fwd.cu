@@ -19,6 +19,7 @@
 //                      src/transformer.rs:259-296; flash_attention, 243-254.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
@@ -64,7 +65,7 @@ struct AttnParams {
   // prefix-fill pass.  NULL: every valid key is visible.
   const int32_t* row_limit;
   float scale_log2;          // scale * log2(e)
-  __nv_bfloat16* out;
+  uint16_t* out;             // 16-bit elements (bf16, or f16 in the kF16 kernel)
   int64_t out_sb, out_sh, out_sr;  // element strides: batch, head, query row
   int32_t* status;
   // Work units.  An item is one (batch, head, 256-row query block); items are numbered
@@ -96,6 +97,21 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Two values rounded to the kernel's 16-bit type (kF16: IEEE half, else bf16), packed.
+template <bool kF16>
+__device__ __forceinline__ uint32_t pack16x2(float lo, float hi) {
+  return kF16 ? pack_f16x2(lo, hi) : pack_bf16x2(lo, hi);
+}
+
+// Quiet NaN of the kernel's 16-bit type, twice.
+template <bool kF16>
+constexpr uint32_t kNaN16x2 = kF16 ? 0x7e007e00u : 0x7fc07fc0u;
 
 __device__ __forceinline__ void named_barrier_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -164,7 +180,7 @@ constexpr int kPolyEvery = 4;
 // which the caller takes after handing P to the MMA warp (off the S -> P critical path).
 // Returns the factor the O accumulator must be scaled by (1 when m did not move).  A row
 // without any valid key so far keeps m = -inf and P = 0.
-template <bool kMasked>
+template <bool kMasked, bool kF16>
 __device__ __forceinline__ float softmax_row(uint32_t (&r)[4][32], const int valid,
                                              const float c, float& m, const uint32_t tS) {
 #pragma unroll
@@ -213,7 +229,7 @@ __device__ __forceinline__ float softmax_row(uint32_t (&r)[4][32], const int val
       }
       r[col >> 5][col & 31] = __float_as_uint(p0);
       r[(col + 1) >> 5][(col + 1) & 31] = __float_as_uint(p1);
-      pk[i] = pack_bf16x2(p0, p1);
+      pk[i] = pack16x2<kF16>(p0, p1);
     }
     tmem_st32(tS + half * 32, pk);
   }
@@ -233,6 +249,9 @@ __device__ __forceinline__ float row_sum(const uint32_t (&r)[4][32]) {
   return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
 }
 
+// kF16: Q, K, V, P and the output are IEEE half (the reference's FA2 branch casts to
+// f16); otherwise bf16.  Accumulation is f32 either way.
+template <bool kF16>
 __global__ void __launch_bounds__(kThreads, 1)
     joint_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_k0,
@@ -414,8 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // and one elected lane issues each tcgen05.mma / commit (always the same lane, so its
     // commits track its own MMAs).
     if (n > 0) {
-      constexpr uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, 0, 0);
-      constexpr uint32_t idesc_pv = idesc_bf16_f32(kBM, kD, 0, 1);
+      constexpr uint32_t idesc_qk = idesc_16_f32(kF16, kBM, kBN, 0, 0);
+      constexpr uint32_t idesc_pv = idesc_16_f32(kF16, kBM, kD, 0, 1);
       // Descriptors as (low, high) words: a k-step only moves the start address (low 14
       // bits, 16-byte units, < 2^14 inside the 256 KiB shared window), so the offset is
       // added to the low word and never carries into the other fields.
@@ -543,8 +562,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the masked path (TMEM loads are warp-collective).
       uint32_t r[4][32];
       const float alpha = __any_sync(0xffffffffu, valid < kBN)
-                              ? softmax_row<true>(r, valid, c, m, tS)
-                              : softmax_row<false>(r, valid, c, m, tS);
+                              ? softmax_row<true, kF16>(r, valid, c, m, tS)
+                              : softmax_row<false, kF16>(r, valid, c, m, tS);
       // O rescale: PV of the previous tile is complete (s_full is committed after it).
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
@@ -566,12 +585,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Epilogue: O / l -> bf16 rows of `out`.
     const int qrow = q0 + t * kBM + row;
     const bool store = qrow < p.T;
-    __nv_bfloat16* dst = p.out + b * p.out_sb + h * p.out_sh + static_cast<int64_t>(qrow) * p.out_sr;
+    uint16_t* dst = p.out + b * p.out_sb + h * p.out_sh + static_cast<int64_t>(qrow) * p.out_sr;
     if (!split_unit) {
       if (n == 0) {
         // No valid key: the reference's softmax over an all -inf row is NaN.
         if (store) {
-          const uint4 nan4 = make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
+          constexpr uint32_t nan2 = kNaN16x2<kF16>;
+          const uint4 nan4 = make_uint4(nan2, nan2, nan2, nan2);
           for (int i = 0; i < kD / 8; ++i) reinterpret_cast<uint4*>(dst)[i] = nan4;
         }
       } else if (ok) {
@@ -588,7 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t w[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-              w[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv_l,
+              w[i] = pack16x2<kF16>(__uint_as_float(o[2 * i]) * inv_l,
                                  __uint_as_float(o[2 * i + 1]) * inv_l);
             if (store) {
               uint4* d4 = reinterpret_cast<uint4*>(dst + q * 32);
@@ -678,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (store) {
             uint32_t w[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(acc[2 * i] * inv_l, acc[2 * i + 1] * inv_l);
+            for (int i = 0; i < 16; ++i) w[i] = pack16x2<kF16>(acc[2 * i] * inv_l, acc[2 * i + 1] * inv_l);
             uint4* d4 = reinterpret_cast<uint4*>(dst + q * 32);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
@@ -878,7 +898,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // 4-D map over a bf16 tensor with 128 columns per row and a 64 x 128-row box, 128-byte
 // swizzle, zero fill outside the tensor.  head_major: [B,H,rows,128] with coordinates
 // (d, row, h, b); otherwise token-major [B,rows,H,128] with coordinates (d, h, row, b).
-int make_map(CUtensorMap* map, const void* base, int B, int H, int rows, bool head_major) {
+int make_map(CUtensorMap* map, const void* base, int B, int H, int rows, bool head_major,
+             bool f16 = false) {
   auto fn = encode_fn();
   if (!fn) return B200_ERR_CUDA;
   cuuint64_t dims[4];
@@ -899,7 +920,8 @@ int make_map(CUtensorMap* map, const void* base, int B, int H, int rows, bool he
     strides[2] = row_bytes * H * rows;
     box[0] = 64; box[1] = 1; box[2] = kBN; box[3] = 1;
   }
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
+  CUresult r = fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                  4, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_CUDA;
@@ -950,7 +972,9 @@ int ensure_kernel_attrs() {
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
   if (major != 10 || minor != 0) return B200_ERR_UNSUPPORTED;
-  if (cudaFuncSetAttribute(joint_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(joint_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kSmemBytes) != cudaSuccess ||
+      cudaFuncSetAttribute(joint_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            kSmemBytes) != cudaSuccess)
     return B200_ERR_CUDA;
   if (dev >= 0 && dev < 64) g_attr_ctx[dev] = current_context_id();
@@ -1004,7 +1028,7 @@ SplitPlan plan_units(int items, int max_tiles, bool have_region) {
 int launch_attention(const CUtensorMap& mq, const CUtensorMap& mk0, const CUtensorMap& mv0,
                      const CUtensorMap& mk1, const CUtensorMap& mv1, AttnParams prm, int B,
                      int H, int T, int max_tiles, void* split_region, cudaStream_t stream,
-                     bool counters_zeroed = false) {
+                     bool counters_zeroed = false, bool f16 = false) {
   int rc = ensure_kernel_attrs();
   if (rc != B200_OK) return rc;
   prm.H = H;
@@ -1023,7 +1047,10 @@ int launch_attention(const CUtensorMap& mq, const CUtensorMap& mk0, const CUtens
     if (!counters_zeroed && cudaMemsetAsync(prm.part_cnt, 0, cnt_bytes, stream) != cudaSuccess)
       return B200_ERR_CUDA;
   }
-  joint_attn_kernel<<<dim3(sp.units), kThreads, kSmemBytes, stream>>>(mq, mk0, mv0, mk1, mv1, prm);
+  if (f16)
+    joint_attn_kernel<true><<<dim3(sp.units), kThreads, kSmemBytes, stream>>>(mq, mk0, mv0, mk1, mv1, prm);
+  else
+    joint_attn_kernel<false><<<dim3(sp.units), kThreads, kSmemBytes, stream>>>(mq, mk0, mv0, mk1, mv1, prm);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
@@ -1083,7 +1110,7 @@ int joint_attention(const void* q_rot, const void* k_rot, const void* v, const v
   prm.seg0_stride = 2;
   prm.seg1_stride = 2;
   prm.scale_log2 = scale * 1.4426950408889634f;
-  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.out = static_cast<uint16_t*>(out);
   prm.out_sb = static_cast<int64_t>(T) * H * kD;
   prm.out_sh = kD;
   prm.out_sr = static_cast<int64_t>(H) * kD;
@@ -1200,7 +1227,7 @@ extern "C" int b200_chunked_attention(const void* q, const void* k, const void* 
   prm.seg1_len = key_len;
   prm.seg1_stride = 1;
   prm.scale_log2 = scale * 1.4426950408889634f;
-  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.out = static_cast<uint16_t*>(out);
   prm.out_sb = static_cast<int64_t>(heads) * sq * kD;
   prm.out_sh = static_cast<int64_t>(sq) * kD;
   prm.out_sr = kD;
@@ -1209,21 +1236,17 @@ extern "C" int b200_chunked_attention(const void* q, const void* k, const void* 
                           nullptr, static_cast<cudaStream_t>(stream_));
 }
 
-extern "C" int b200_flash_attention(const void* q, const void* k, const void* v, void* out,
-                                    int32_t batch, int32_t sq, int32_t skv, int32_t heads,
-                                    int32_t head_dim, float scale, const int32_t* key_len,
-                                    int32_t* status, b200_stream_t stream_) {
-  if (head_dim != kD) return B200_ERR_UNSUPPORTED;
-  if (batch <= 0 || heads <= 0 || sq < 0 || skv <= 0) return B200_ERR_INVALID;
-  if (sq == 0) return B200_OK;
-  if (!q || !k || !v || !out) return B200_ERR_INVALID;
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return B200_ERR_INVALID;
-  if (!(scale > 0.f) || !std::isfinite(scale)) return B200_ERR_INVALID;
+namespace {
+// flash_attn(q, k, v, scale, causal = false) on token-major [B,S,H,D] tensors of either
+// 16-bit type; arguments validated by the callers.
+int flash_attention_impl(const void* q, const void* k, const void* v, void* out, int32_t batch,
+                         int32_t sq, int32_t skv, int32_t heads, float scale,
+                         const int32_t* key_len, int32_t* status, cudaStream_t stream, bool f16) {
   CUtensorMap mq{}, mk0{}, mv0{}, mk1{}, mv1{};
   int rc;
-  if ((rc = make_map(&mq, q, batch, heads, sq, false)) != B200_OK) return rc;
-  if ((rc = make_map(&mk1, k, batch, heads, skv, false)) != B200_OK) return rc;
-  if ((rc = make_map(&mv1, v, batch, heads, skv, false)) != B200_OK) return rc;
+  if ((rc = make_map(&mq, q, batch, heads, sq, false, f16)) != B200_OK) return rc;
+  if ((rc = make_map(&mk1, k, batch, heads, skv, false, f16)) != B200_OK) return rc;
+  if ((rc = make_map(&mv1, v, batch, heads, skv, false, f16)) != B200_OK) return rc;
   AttnParams prm{};
   prm.T = sq;
   prm.P = 0;
@@ -1234,13 +1257,48 @@ extern "C" int b200_flash_attention(const void* q, const void* k, const void* v,
   prm.seg1_len = key_len;
   prm.seg1_stride = 1;
   prm.scale_log2 = scale * 1.4426950408889634f;
-  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.out = static_cast<uint16_t*>(out);
   prm.out_sb = static_cast<int64_t>(sq) * heads * kD;
   prm.out_sh = kD;
   prm.out_sr = static_cast<int64_t>(heads) * kD;
   prm.status = status;
   return launch_attention(mq, mk0, mv0, mk1, mv1, prm, batch, heads, sq, (skv + kBN - 1) / kBN,
-                          nullptr, static_cast<cudaStream_t>(stream_));
+                          nullptr, stream, false, f16);
+}
+
+int flash_attention_check(const void* q, const void* k, const void* v, void* out,
+                          int32_t batch, int32_t sq, int32_t skv, int32_t heads,
+                          int32_t head_dim, float scale) {
+  if (head_dim != kD) return B200_ERR_UNSUPPORTED;
+  if (batch <= 0 || heads <= 0 || sq < 0 || skv <= 0) return B200_ERR_INVALID;
+  if (!q || !k || !v || !out) return B200_ERR_INVALID;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return B200_ERR_INVALID;
+  if (!(scale > 0.f) || !std::isfinite(scale)) return B200_ERR_INVALID;
+  return B200_OK;
+}
+}  // namespace
+
+extern "C" int b200_flash_attention(const void* q, const void* k, const void* v, void* out,
+                                    int32_t batch, int32_t sq, int32_t skv, int32_t heads,
+                                    int32_t head_dim, float scale, const int32_t* key_len,
+                                    int32_t* status, b200_stream_t stream_) {
+  if (head_dim == kD && batch > 0 && heads > 0 && sq == 0 && skv > 0) return B200_OK;
+  const int rc = flash_attention_check(q, k, v, out, batch, sq, skv, heads, head_dim, scale);
+  if (rc != B200_OK) return rc;
+  return flash_attention_impl(q, k, v, out, batch, sq, skv, heads, scale, key_len, status,
+                              static_cast<cudaStream_t>(stream_), false);
+}
+
+extern "C" int b200_flash_attention_ex(const void* q, const void* k, const void* v, void* out,
+                                       int32_t batch, int32_t sq, int32_t skv, int32_t heads,
+                                       int32_t head_dim, float scale, const int32_t* key_len,
+                                       int32_t dtype, int32_t* status, b200_stream_t stream_) {
+  if (dtype != B200_DTYPE_BF16 && dtype != B200_DTYPE_F16) return B200_ERR_UNSUPPORTED;
+  if (head_dim == kD && batch > 0 && heads > 0 && sq == 0 && skv > 0) return B200_OK;
+  const int rc = flash_attention_check(q, k, v, out, batch, sq, skv, heads, head_dim, scale);
+  if (rc != B200_OK) return rc;
+  return flash_attention_impl(q, k, v, out, batch, sq, skv, heads, scale, key_len, status,
+                              static_cast<cudaStream_t>(stream_), dtype == B200_DTYPE_F16);
 }
 
 extern "C" int b200_norm_rope(const void* x, void* y, int32_t batch, int32_t tokens,

@@ -288,6 +288,15 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t m, uint32_t n, ui
          | (a_mn << 15) | (b_mn << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
+// Instruction descriptor of kind::f16 with A/B both f16 (f16 = true) or both bf16, f32 D.
+__host__ __device__ constexpr uint32_t idesc_16_f32(bool f16, uint32_t m, uint32_t n,
+                                                    uint32_t a_mn, uint32_t b_mn) {
+  return (1u << 4)                      // D format f32
+         | ((f16 ? 0u : 1u) << 7)       // A format: 0 = f16, 1 = bf16
+         | ((f16 ? 0u : 1u) << 10)      // B format
+         | (a_mn << 15) | (b_mn << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

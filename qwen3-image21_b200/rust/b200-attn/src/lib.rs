@@ -19,9 +19,14 @@ pub mod ffi {
     use std::ffi::{c_char, c_int, c_void};
 
     pub const B200_ATTN_HEAD_DIM: i32 = 128;
-    pub const B200_ATTN_ABI_VERSION: i32 = 3;
+    pub const B200_ATTN_ABI_VERSION: i32 = 4;
     pub const B200_ATTN_SPLIT_WORKSPACE_BYTES: usize = 21299968;
     pub const B200_NOALLOC_SCRATCH_BYTES: usize = 64 << 20;
+
+    /// `b200_dtype`: element types of the entry points that take more than one.
+    pub const B200_DTYPE_BF16: i32 = 0;
+    pub const B200_DTYPE_F32: i32 = 1;
+    pub const B200_DTYPE_F16: i32 = 2;
 
     pub const B200_OK: c_int = 0;
     pub const B200_ERR_INVALID: c_int = -1;
@@ -82,6 +87,10 @@ pub mod ffi {
         pub fn b200_flash_attention(q: *const c_void, k: *const c_void, v: *const c_void,
             out: *mut c_void, batch: i32, sq: i32, skv: i32, heads: i32, head_dim: i32,
             scale: f32, key_len: *const i32, status: *mut i32, stream: *mut c_void) -> c_int;
+        pub fn b200_flash_attention_ex(q: *const c_void, k: *const c_void, v: *const c_void,
+            out: *mut c_void, batch: i32, sq: i32, skv: i32, heads: i32, head_dim: i32,
+            scale: f32, key_len: *const i32, dtype: i32, status: *mut i32,
+            stream: *mut c_void) -> c_int;
         pub fn b200_chunked_attention(q: *const c_void, k: *const c_void, v: *const c_void,
             out: *mut c_void, batch: i32, heads: i32, sq: i32, skv: i32, head_dim: i32,
             scale: f32, key_len: *const i32, status: *mut i32, stream: *mut c_void) -> c_int;
@@ -141,7 +150,7 @@ pub fn check(rc: c_int) -> Result<()> {
     if rc == ffi::B200_OK { Ok(()) } else { Err(Error { status: rc, message: message(rc) }) }
 }
 
-/// The ABI version the loaded library was built with (3 for this binding).
+/// The ABI version the loaded library was built with (4 for this binding).
 pub fn abi_version() -> i32 {
     unsafe { ffi::b200_abi_version() }
 }

@@ -140,6 +140,18 @@ def test_entry_points_reject_bad_arguments_without_device():
                                     None) == b200attn.OK  # nothing to do
     assert lib.b200_flash_attention(16, 16, 16, 16, 1, 4, 4, 1, 128, -1.0, None, None,
                                     None) == b200attn.ERR_INVALID
+    # b200_flash_attention_ex: bf16 and f16 pass the checks, any other element type (f32,
+    # an unknown code) is refused before anything else is looked at
+    for dt in (b200attn.DTYPE_F32, 7, -1):
+        assert lib.b200_flash_attention_ex(16, 16, 16, 16, 1, 4, 4, 1, 128, 0.1, None, dt, None,
+                                           None) == b200attn.ERR_UNSUPPORTED
+    for dt in (b200attn.DTYPE_BF16, b200attn.DTYPE_F16):
+        assert lib.b200_flash_attention_ex(None, None, None, None, 1, 4, 4, 1, 128, 0.1, None, dt,
+                                           None, None) == b200attn.ERR_INVALID
+        assert lib.b200_flash_attention_ex(16, 16, 16, 16, 1, 4, 4, 1, 64, 0.1, None, dt, None,
+                                           None) == b200attn.ERR_UNSUPPORTED
+        assert lib.b200_flash_attention_ex(16, 16, 16, 16, 1, 0, 4, 1, 128, 0.1, None, dt, None,
+                                           None) == b200attn.OK  # nothing to do
 
 
 def test_workspace_bytes():

@@ -151,6 +151,50 @@ def test_flash_attention_bshd_matches_oracle(cuda, B, H, sq, skv, lens):
     check(np.transpose(f32np(out), (0, 2, 1, 3)), want)
 
 
+@pytest.mark.parametrize("B,H,sq,skv,lens", [
+    (1, 2, 256, 256, None), (2, 3, 37, 300, None),
+    (2, 2, 300, 4608, [4608, 4581]),
+    (3, 1, 129, 200, [1, 128, 200]),
+])
+def test_flash_attention_f16_matches_oracle(cuda, B, H, sq, skv, lens):
+    """The FA2 branch in the type the reference casts to (IEEE half, src/transformer.rs:
+    244-251): f16 q/k/v in, f16 out, against the oracle on the same f16 values."""
+    torch = _torch()
+    g = torch.Generator().manual_seed(B * 13 + H * 5 + sq + skv)
+    q = torch.randn(B, sq, H, 128, generator=g).half()
+    k = torch.randn(B, skv, H, 128, generator=g).half()
+    v = torch.randn(B, skv, H, 128, generator=g).half()
+    key_len = None if lens is None else torch.tensor(lens, dtype=torch.int32, device=cuda)
+    out = b200attn.flash_attention(q.to(cuda), k.to(cuda), v.to(cuda), 128 ** -0.5,
+                                   key_len=key_len)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float16
+    mask = None
+    if lens is not None:
+        mask = np.zeros((B, 1, 1, skv), bool)
+        for b, n in enumerate(lens):
+            mask[b, ..., :n] = True
+    t = lambda x: np.transpose(f32np(x), (0, 2, 1, 3))
+    want = ref.chunked_attention(t(q), t(k), t(v), 128 ** -0.5, mask)
+    # f16 carries 3 more mantissa bits than bf16: the same bar, met with room to spare
+    r, _ = check(np.transpose(f32np(out), (0, 2, 1, 3)), want)
+    assert r < 1.5e-3
+    # the bf16 entry point on the same values (rounded to bf16) agrees to bf16 precision
+    out_bf = b200attn.flash_attention(bf16(q.float()).to(cuda), bf16(k.float()).to(cuda),
+                                      bf16(v.float()).to(cuda), 128 ** -0.5, key_len=key_len)
+    torch.cuda.synchronize()
+    check(f32np(out_bf), f32np(out), rel=1e-2, mx=3e-2)
+
+
+def test_flash_attention_rejects_other_dtypes(cuda):
+    torch = _torch()
+    q = torch.zeros(1, 16, 1, 128, device=cuda, dtype=torch.float32)
+    with pytest.raises(b200attn.B200Error) as e:
+        b200attn.flash_attention(q, q, q, 0.1, out=torch.empty(1, 16, 1, 128, device=cuda,
+                                                                 dtype=torch.float16))
+    assert e.value.status == b200attn.ERR_UNSUPPORTED
+
+
 def test_chunked_attention_key_mask(cuda):
     torch = _torch()
     g = torch.Generator().manual_seed(5)
