@@ -115,6 +115,9 @@ def parse_args():
                     help="config 5: the block linears' GEMM (cuBLAS or the tcgen05 kernel)")
     ap.add_argument("--fused-qkv", action="store_true",
                     help="config 5: Q/K/V projections with norm + RoPE in the GEMM epilogue")
+    ap.add_argument("--no-weight-prefetch", action="store_true",
+                    help="config 5 (q4_k_m): dequantise each block's weights on the compute "
+                         "stream instead of one block ahead on a side stream")
     return ap.parse_args()
 
 
@@ -1003,7 +1006,8 @@ def run_denoise(args, cfg, rank, world, dev, leg=False):
     lengths = [n for p in mine for n in pairs[p]]          # p0 pos, p0 neg, p1 pos, ...
     weights = mmdit.random_weights(mcfg, 2024, device=dev, std=0.02)   # same on every rank
     model = mmdit.MMDiT(mcfg, weights, device=dev, weight_format=args.weights,
-                        fused_qkv=args.fused_qkv, gemm=args.gemm)
+                        fused_qkv=args.fused_qkv, gemm=args.gemm,
+                        prefetch_weights=not args.no_weight_prefetch)
     del weights
     torch.cuda.empty_cache()
     wbytes = model.weight_bytes()

@@ -186,7 +186,8 @@ class MMDiT:
     """The transformer on one GPU with bf16 weights (see module docstring)."""
 
     def __init__(self, cfg: MMDiTConfig, weights: dict, device="cuda", mlp_chunk_rows: int = 16384,
-                 weight_format: str = "bf16", fused_qkv: bool = False, gemm: str = "cublas"):
+                 weight_format: str = "bf16", fused_qkv: bool = False, gemm: str = "cublas",
+                 prefetch_weights: bool = True):
         """weight_format "bf16" keeps the block linears in bf16; "q4_k_m" stores them as GGUF
         Q4_K / Q6_K super-blocks (llama.cpp's Q4_K_M rule) and dequantises each block's six
         matrices to a bf16 scratch right before its GEMMs.  The other weights (img_in,
@@ -195,7 +196,9 @@ class MMDiT:
         Q/K RMSNorm + RoPE in the GEMM epilogue (b200_qkv_norm_rope_gemm) and then the
         attention kernel alone; otherwise (the default, 1.3 % faster at config 5 while the
         tcgen05 GEMM runs the 12288-wide projection at ~90 % of cuBLAS) three cuBLAS GEMMs
-        and b200_attn_fwd."""
+        and b200_attn_fwd.  prefetch_weights (q4_k_m): dequantise block i + 1's linears on a
+        side stream while block i computes (two scratch slots); off, each block's are
+        dequantised on the compute stream right before its GEMMs."""
         import torch
         if weight_format not in ("bf16", "q4_k_m"):
             raise ValueError(f"unknown weight format {weight_format!r}")
@@ -206,6 +209,7 @@ class MMDiT:
         self.mlp_chunk_rows = mlp_chunk_rows
         self.weight_format = weight_format
         self.fused_qkv = fused_qkv
+        self.prefetch_weights = prefetch_weights
         dev = self.device
         bf = lambda n: weights[n].to(device=dev, dtype=torch.bfloat16).contiguous()
         f32 = lambda n: weights[n].to(device=dev, dtype=torch.float32).contiguous()
@@ -300,23 +304,32 @@ class MMDiT:
         import torch.nn.functional as F
         return F.silu(t_emb) @ self.norm_out_w.t()
 
-    def block_weights(self, i: int) -> dict:
+    def block_weights(self, i: int, slot: int = 0, stream=None) -> dict:
         """Block i's bf16 weights: the stored tensors, or (q4_k_m) its six linears
-        dequantised into this model's scratch buffers (valid until the next call)."""
+        dequantised into this model's scratch slot `slot` on `stream` (valid until the slot
+        is filled again)."""
         import torch
         blk = self.blocks[i]
         if self.weight_format == "bf16":
             return blk
         out = dict(nq=blk["nq"], nk=blk["nk"])
         h = self.cfg.hidden
-        wqkv = self._buf("dq_wqkv", (3 * h, h), torch.bfloat16)
+        wqkv = self._buf(f"dq{slot}_wqkv", (3 * h, h), torch.bfloat16)
         for j, key in enumerate(("wq", "wk", "wv")):
-            out[key] = blk["q_" + key].dequant_into(wqkv[j * h:(j + 1) * h])
+            out[key] = blk["q_" + key].dequant_into(wqkv[j * h:(j + 1) * h], stream=stream)
         out["wqkv"] = wqkv
         for key in ("wo", "wgp", "wmo"):
             ql = blk["q_" + key]
-            out[key] = ql.dequant_into(self._buf("dq_" + key, ql.shape, torch.bfloat16))
+            out[key] = ql.dequant_into(self._buf(f"dq{slot}_" + key, ql.shape, torch.bfloat16),
+                                       stream=stream)
         return out
+
+    def _dq_stream(self):
+        """Side stream that dequantises the next block's weights during this block."""
+        import torch
+        if getattr(self, "_dq", None) is None:
+            self._dq = torch.cuda.Stream(self.device)
+        return self._dq
 
     def weight_bytes(self) -> int:
         """HBM bytes of the block linears (the 99 % of the parameters they hold)."""
@@ -409,8 +422,35 @@ class MMDiT:
             sink = self._staging("out", kv_out.k[0].shape)
             computed = [torch.cuda.Event() for _ in range(2)]
             drained = [None, None]
+        # Q4_K_M weights: block i + 1's six linears are dequantised into the other scratch
+        # slot on a side stream while block i computes (the dequantisation reads HBM, the
+        # block's GEMMs keep the tensor cores busy); a slot is refilled only after the
+        # block that read it is done.
+        quant = self.weight_format == "q4_k_m" and self.prefetch_weights
+        if quant:
+            dq = self._dq_stream()
+            w_ready = [torch.cuda.Event(), torch.cuda.Event()]
+            w_free = [None, None]
+            dq.wait_stream(cur)  # earlier work on the scratch slots is ordered first
+
+            def fetch(layer):
+                sl = layer % 2
+                if w_free[sl] is not None:
+                    dq.wait_event(w_free[sl])
+                with torch.cuda.stream(dq):
+                    w = self.block_weights(layer, sl, stream=dq)
+                    w_ready[sl].record(dq)
+                return w
+
+            nxt = fetch(0)
         for i in range(len(self.blocks)):
-            blk = self.block_weights(i)
+            if quant:
+                blk = nxt
+                cur.wait_event(w_ready[i % 2])
+                if i + 1 < len(self.blocks):
+                    nxt = fetch(i + 1)
+            else:
+                blk = self.block_weights(i)
             pk = pv = None
             if staged is not None:
                 if i + 1 < len(self.blocks):
@@ -471,6 +511,10 @@ class MMDiT:
                 hh = b200attn.swiglu(gp, self._buf("h", (r1 - r0, cfg.ffn), torch.bfloat16))
                 self._gemm(hh, blk["wmo"], "mo", out=mo[r0:r1])
             last = i + 1 == len(self.blocks)
+            if quant:
+                # (the residual kernel below reads no weights; the slot is free after mo)
+                w_free[i % 2] = torch.cuda.Event()
+                w_free[i % 2].record(cur)
             if last and sink is not None:
                 for ev in drained:  # the host cache is complete when the pass is
                     if ev is not None:
