@@ -15,7 +15,8 @@
 //                      fill, per-row limits); the last partial wave of work items can be
 //                      cut by key range (tail split) and merged by the last piece.  Q, K
 //                      and V are read through 4-D tensor maps either head-major or
-//                      token-major.  Reference: chunked_attention,
+//                      token-major.  The output tile is staged in the Q slot of shared
+//                      memory and written by TMA stores.  Reference: chunked_attention,
 //                      src/transformer.rs:259-296; flash_attention, 243-254.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -57,6 +58,7 @@ struct AttnParams {
   int32_t v1_token_major;    // segment-1 V map is [B,T,H,D] (coords d, h, row, b)
   int32_t k1_token_major;    // segment-1 K map is [B,T,H,D] (coords d, h, row, b)
   int32_t q_token_major;     // Q map is [B,T,H,D] (coords d, h, row, b)
+  int32_t o_token_major;     // output map is [B,T,H,D] (coords d, h, row, b)
   const int32_t* seg0_len;   // valid keys of segment 0 per batch row (stride seg0_stride)
   const int32_t* seg1_len;
   int32_t seg0_stride, seg1_stride;
@@ -257,7 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tm_k0,
                       const __grid_constant__ CUtensorMap tm_v0,
                       const __grid_constant__ CUtensorMap tm_k1,
-                      const __grid_constant__ CUtensorMap tm_v1, const AttnParams p) {
+                      const __grid_constant__ CUtensorMap tm_v1,
+                      const __grid_constant__ CUtensorMap tm_o, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -594,29 +597,51 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint4 nan4 = make_uint4(nan2, nan2, nan2, nan2);
           for (int i = 0; i < kD / 8; ++i) reinterpret_cast<uint4*>(dst)[i] = nan4;
         }
-      } else if (ok) {
-        if (!wait_or_abort(o_full + t, 0, abort_flag)) {
+      } else {
+        // O row -> this tile's Q slot in shared memory (free: every MMA that read Q is
+        // complete once o_full is), in the 128-byte-swizzled layout of the output tensor
+        // map's 64-column boxes; then one thread writes the tile with two TMA stores (rows
+        // past T are clipped by the map).  The named barrier is reached by all 128 threads
+        // of the tile on every path.
+        bool have = ok;
+        if (have && !wait_or_abort(o_full + t, 0, abort_flag)) {
           record_error(p, abort_flag, 4);
-        } else {
+          have = false;
+        }
+        have = __all_sync(0xffffffffu, have);  // TMEM loads are warp-collective
+        uint8_t* stg = sQ + t * kTileBytes;
+        if (have) {
           tc_fence_after();
           const float inv_l = 1.f / l;
+          uint32_t o[4][32];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t o[32];
-            tmem_ld32(tO + q * 32, o);
-            tmem_wait_ld();
-            uint32_t w[16];
+          for (int q = 0; q < 4; ++q) tmem_ld32(tO + q * 32, o[q]);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              w[i] = pack16x2<kF16>(__uint_as_float(o[2 * i]) * inv_l,
-                                 __uint_as_float(o[2 * i + 1]) * inv_l);
-            if (store) {
-              uint4* d4 = reinterpret_cast<uint4*>(dst + q * 32);
-#pragma unroll
-              for (int i = 0; i < 4; ++i)
-                d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-            }
+          for (int c16 = 0; c16 < 16; ++c16) {  // 16-byte chunk = 8 output columns
+            const int q = c16 >> 2, i0 = (c16 & 3) * 8;
+            const uint4 v4 = make_uint4(
+                pack16x2<kF16>(__uint_as_float(o[q][i0]) * inv_l, __uint_as_float(o[q][i0 + 1]) * inv_l),
+                pack16x2<kF16>(__uint_as_float(o[q][i0 + 2]) * inv_l, __uint_as_float(o[q][i0 + 3]) * inv_l),
+                pack16x2<kF16>(__uint_as_float(o[q][i0 + 4]) * inv_l, __uint_as_float(o[q][i0 + 5]) * inv_l),
+                pack16x2<kF16>(__uint_as_float(o[q][i0 + 6]) * inv_l, __uint_as_float(o[q][i0 + 7]) * inv_l));
+            const int region = c16 >> 3, chunk = c16 & 7;
+            *reinterpret_cast<uint4*>(stg + region * kRegionBytes + row * 128 +
+                                      ((chunk ^ (row & 7)) << 4)) = v4;
           }
+        }
+        fence_proxy_async();
+        named_barrier_sync(2 + t, kBM);
+        if (wq == 0 && lane == 0 && have) {
+          const int r0 = q0 + t * kBM;
+          for (int c = 0; c < 2; ++c) {
+            if (p.o_token_major)
+              tma_store_4d(&tm_o, stg + c * kRegionBytes, c * 64, h, r0, b);
+            else
+              tma_store_4d(&tm_o, stg + c * kRegionBytes, c * 64, r0, h, b);
+          }
+          bulk_commit();
+          bulk_wait_read0();  // the shared-memory source stays valid until read
         }
       }
     } else {
@@ -1026,7 +1051,8 @@ SplitPlan plan_units(int items, int max_tiles, bool have_region) {
 
 // Fills the work-unit fields of prm (split region optional) and launches.
 int launch_attention(const CUtensorMap& mq, const CUtensorMap& mk0, const CUtensorMap& mv0,
-                     const CUtensorMap& mk1, const CUtensorMap& mv1, AttnParams prm, int B,
+                     const CUtensorMap& mk1, const CUtensorMap& mv1, const CUtensorMap& mo,
+                     AttnParams prm, int B,
                      int H, int T, int max_tiles, void* split_region, cudaStream_t stream,
                      bool counters_zeroed = false, bool f16 = false) {
   int rc = ensure_kernel_attrs();
@@ -1048,9 +1074,9 @@ int launch_attention(const CUtensorMap& mq, const CUtensorMap& mk0, const CUtens
       return B200_ERR_CUDA;
   }
   if (f16)
-    joint_attn_kernel<true><<<dim3(sp.units), kThreads, kSmemBytes, stream>>>(mq, mk0, mv0, mk1, mv1, prm);
+    joint_attn_kernel<true><<<dim3(sp.units), kThreads, kSmemBytes, stream>>>(mq, mk0, mv0, mk1, mv1, mo, prm);
   else
-    joint_attn_kernel<false><<<dim3(sp.units), kThreads, kSmemBytes, stream>>>(mq, mk0, mv0, mk1, mv1, prm);
+    joint_attn_kernel<false><<<dim3(sp.units), kThreads, kSmemBytes, stream>>>(mq, mk0, mv0, mk1, mv1, mo, prm);
   return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
 }
 
@@ -1090,9 +1116,10 @@ int joint_attention(const void* q_rot, const void* k_rot, const void* v, const v
                     float scale, void* out, int32_t* status, void* split_region,
                     cudaStream_t stream, bool counters_zeroed = false,
                     const int32_t* row_limit = nullptr) {
-  CUtensorMap mq{}, mk0{}, mv0{}, mk1{}, mv1{};
+  CUtensorMap mq{}, mk0{}, mv0{}, mk1{}, mv1{}, mo{};
   int rc;
   if ((rc = make_map(&mq, q_rot, B, H, T, true)) != B200_OK) return rc;
+  if ((rc = make_map(&mo, out, B, H, T, false)) != B200_OK) return rc;
   if ((rc = make_map(&mk1, k_rot, B, H, T, true)) != B200_OK) return rc;
   if ((rc = make_map(&mv1, v, B, H, T, false)) != B200_OK) return rc;
   if (P > 0) {
@@ -1116,7 +1143,8 @@ int joint_attention(const void* q_rot, const void* k_rot, const void* v, const v
   prm.out_sr = static_cast<int64_t>(H) * kD;
   prm.status = status;
   const int max_tiles = (P + kBN - 1) / kBN + (T + kBN - 1) / kBN;
-  return launch_attention(mq, mk0, mv0, mk1, mv1, prm, B, H, T, max_tiles, split_region, stream,
+  prm.o_token_major = 1;
+  return launch_attention(mq, mk0, mv0, mk1, mv1, mo, prm, B, H, T, max_tiles, split_region, stream,
                           counters_zeroed);
 }
 
@@ -1214,9 +1242,10 @@ extern "C" int b200_chunked_attention(const void* q, const void* k, const void* 
   if (!q || !k || !v || !out) return B200_ERR_INVALID;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return B200_ERR_INVALID;
   if (!(scale > 0.f) || !std::isfinite(scale)) return B200_ERR_INVALID;
-  CUtensorMap mq{}, mk0{}, mv0{}, mk1{}, mv1{};
+  CUtensorMap mq{}, mk0{}, mv0{}, mk1{}, mv1{}, mo{};
   int rc;
   if ((rc = make_map(&mq, q, batch, heads, sq, true)) != B200_OK) return rc;
+  if ((rc = make_map(&mo, out, batch, heads, sq, true)) != B200_OK) return rc;
   if ((rc = make_map(&mk1, k, batch, heads, skv, true)) != B200_OK) return rc;
   if ((rc = make_map(&mv1, v, batch, heads, skv, true)) != B200_OK) return rc;
   AttnParams prm{};
@@ -1232,7 +1261,8 @@ extern "C" int b200_chunked_attention(const void* q, const void* k, const void* 
   prm.out_sh = static_cast<int64_t>(sq) * kD;
   prm.out_sr = kD;
   prm.status = status;
-  return launch_attention(mq, mk0, mv0, mk1, mv1, prm, batch, heads, sq, (skv + kBN - 1) / kBN,
+  prm.o_token_major = 0;
+  return launch_attention(mq, mk0, mv0, mk1, mv1, mo, prm, batch, heads, sq, (skv + kBN - 1) / kBN,
                           nullptr, static_cast<cudaStream_t>(stream_));
 }
 
@@ -1242,9 +1272,10 @@ namespace {
 int flash_attention_impl(const void* q, const void* k, const void* v, void* out, int32_t batch,
                          int32_t sq, int32_t skv, int32_t heads, float scale,
                          const int32_t* key_len, int32_t* status, cudaStream_t stream, bool f16) {
-  CUtensorMap mq{}, mk0{}, mv0{}, mk1{}, mv1{};
+  CUtensorMap mq{}, mk0{}, mv0{}, mk1{}, mv1{}, mo{};
   int rc;
   if ((rc = make_map(&mq, q, batch, heads, sq, false, f16)) != B200_OK) return rc;
+  if ((rc = make_map(&mo, out, batch, heads, sq, false, f16)) != B200_OK) return rc;
   if ((rc = make_map(&mk1, k, batch, heads, skv, false, f16)) != B200_OK) return rc;
   if ((rc = make_map(&mv1, v, batch, heads, skv, false, f16)) != B200_OK) return rc;
   AttnParams prm{};
@@ -1262,7 +1293,8 @@ int flash_attention_impl(const void* q, const void* k, const void* v, void* out,
   prm.out_sh = kD;
   prm.out_sr = static_cast<int64_t>(heads) * kD;
   prm.status = status;
-  return launch_attention(mq, mk0, mv0, mk1, mv1, prm, batch, heads, sq, (skv + kBN - 1) / kBN,
+  prm.o_token_major = 1;
+  return launch_attention(mq, mk0, mv0, mk1, mv1, mo, prm, batch, heads, sq, (skv + kBN - 1) / kBN,
                           nullptr, stream, false, f16);
 }
 
