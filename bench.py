@@ -826,6 +826,38 @@ def run_head_sharded(args, cfg, rank, world, dev):
         ms_fused = timed(step_fused, args.steps, marks)
     attn_ms = sum(m[0].elapsed_time(m[1]) for m in marks) / args.steps
     ms_nccl = timed(step_nccl, args.steps)
+    # ---- the block's next steps fused into the owners' step: x += tanh(gate1) * to_out and
+    # norm2(x) * (1 + scale2) (src/transformer.rs:411-421).  Timed against the same work
+    # done after the gather / all-reduce by the residual_adaln kernel over all T rows.
+    res_ms = None
+    if fused is not None:
+        x_full = torch.randn(T, hidden, generator=g, device=dev, dtype=torch.float32)
+        gate = torch.randn(1, hidden, generator=g, device=dev, dtype=torch.float32)
+        scale = 0.5 * torch.randn(1, hidden, generator=g, device=dev, dtype=torch.float32)
+        r0, mine = fused.own_rows(T)
+        x_own = x_full[r0:r0 + mine].clone()
+        y_full = torch.empty(T, hidden, dtype=torch.bfloat16, device=dev)
+
+        def step_res_owner(mark=None):
+            return fused(attention(), w_out, h0, h1, status=status,
+                         residual=(x_own, gate, scale))
+
+        def step_res_after(tail):
+            def run(mark=None):
+                y = tail(attention())
+                b200attn.residual_adaln(x_full, y, gate, scale, y_full, rows_per_mod=T,
+                                        stream=stream)
+                return y_full
+            return run
+
+        legs = dict(owner_step=step_res_owner,
+                    fused_then_residual_adaln=step_res_after(
+                        lambda a: fused(a, w_out, h0, h1, status=status)),
+                    nccl_then_residual_adaln=step_res_after(step_nccl_tail))
+        for fn in legs.values():
+            for _ in range(2):
+                fn()
+        res_ms = {name: timed(fn, args.steps) for name, fn in legs.items()}
     if int(status.item()) != 0:
         raise RuntimeError(f"device wait ran out during the bench (status {int(status.item())})")
     # ---- end to end through the public calls with host buffers: this rank's q/k/v of a
@@ -889,6 +921,8 @@ def run_head_sharded(args, cfg, rank, world, dev):
     e2e_ms = bdist.max_over_ranks(e2e["ms"], device=dev) if e2e else None
     ms_step = ms_fused if use_fused else ms_nccl
     attn_ms = bdist.max_over_ranks(attn_ms, device=dev)
+    if res_ms is not None:
+        res_ms = {k: bdist.max_over_ranks(v, device=dev) for k, v in res_ms.items()}
     attn_flops = 4.0 * HEADS * T * (P + T) * HEAD_DIM
     proj_flops = 2.0 * T * HEADS * HEAD_DIM * hidden
     if rank == 0:
@@ -915,6 +949,10 @@ def run_head_sharded(args, cfg, rank, world, dev):
                           "value": (attn_flops + proj_flops) / (ms_nccl / 1e3) / 1e12,
                           "how": "cuBLAS to_out partial + NCCL all-reduce (bf16)"},
             "fused_path": {"ms_per_step": ms_fused, "how": fused_note},
+            "with_residual_norm2": None if res_ms is None else dict(
+                res_ms, how=("step + x += tanh(gate1) * to_out + norm2 * (1 + scale2): in the "
+                             "owners' reduce step (owner_step) vs a residual_adaln kernel over "
+                             "all rows after the sum (ms per step, max over ranks)")),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak,
                          # captured with all 32 heads on one GPU; a rank's launch moves its

@@ -68,6 +68,26 @@ int b200_reduce_gather_bf16(const void* slots, int32_t n_src, int32_t slot_rows,
                             int64_t dst_row0, int64_t dst_ld, b200_stream_t stream);
 
 /*
+ * The owner's step of a head-sharded block with the tanh-gated residual and the next
+ * modulated LayerNorm fused in: for r < rows (<= slot_rows),
+ *   sum       = sum over s < n_src of slots[s * slot_rows + r, :]   (f32, fixed order)
+ *   x[r, :]  += tanh(gate[m, :]) * sum                              (f32, in place)
+ *   out[dst_row0 + r, :] = bf16(LN(x[r, :]) * (1 + scale[m, :]))   into every dst buffer
+ * with m = (dst_row0 + r) / rows_per_mod (gate / scale rows mod_stride floats apart) and LN
+ * the reference's affine-free LayerNorm (eps).  x [rows, ldx] f32 holds the owner's rows of
+ * the residual stream (the stream is split over the ranks like the reduce-scatter); the
+ * bf16 result, all-gathered, is the next GEMM's input.  Replaces, for the head-sharded
+ * block, the sum of the to_out partials followed by `x + tanh(gate1) * attn` and
+ * `norm2(x) * (1 + scale2)` (src/transformer.rs:196, 411-418).  cols % 8 == 0, cols <= 8192.
+ */
+int b200_reduce_residual_adaln_gather(const void* slots, int32_t n_src, int32_t slot_rows,
+                                      int32_t rows, int32_t cols, int64_t ld, float* x,
+                                      int64_t ldx, const float* gate, const float* scale,
+                                      int64_t rows_per_mod, int64_t mod_stride, float eps,
+                                      void* const* dst_bufs, int32_t n_dst, int64_t dst_row0,
+                                      int64_t dst_ld, b200_stream_t stream);
+
+/*
  * The Q/K/V projections of one attention layer with the Q/K RMSNorm and RoPE in the
  * GEMM's epilogue: x [B * T, in_features] bf16 (row stride ldx) times w_qkv
  * [3 * H * 128, in_features] bf16 (to_q, to_k, to_v stacked) transposed, then

@@ -37,7 +37,8 @@ EXPORTED = (
     "b200_strerror", "b200_attn_strerror", "b200_abi_version",
     "b200_residual_adaln", "b200_swiglu",
     "b200_dequant_q4_k", "b200_dequant_q6_k", "b200_wait_selftest", "b200_gemm",
-    "b200_gemm_scatter", "b200_reduce_gather_bf16", "b200_qkv_norm_rope_gemm",
+    "b200_gemm_scatter", "b200_reduce_gather_bf16", "b200_reduce_residual_adaln_gather",
+    "b200_qkv_norm_rope_gemm",
     "b200_tp_unique_id", "b200_tp_init", "b200_tp_init_from_nccl", "b200_tp_rank", "b200_tp_size",
     "b200_tp_out_proj_allreduce", "b200_tp_wait", "b200_tp_destroy",
 )
@@ -105,6 +106,8 @@ def lib() -> ctypes.CDLL:
         L.b200_gemm.argtypes = [vp, i64, vp, i64, vp, i64, i32, i32, i32, i32, vp, vp]
         L.b200_gemm_scatter.argtypes = [vp, i64, vp, i64, vp, i32, i32, i32, i64, i32, i32, i32, vp, vp]
         L.b200_reduce_gather_bf16.argtypes = [vp, i32, i32, i32, i32, i64, vp, i32, i64, i64, vp]
+        L.b200_reduce_residual_adaln_gather.argtypes = [vp, i32, i32, i32, i32, i64, vp, i64, vp, vp,
+                                                        i64, i64, f32, vp, i32, i64, i64, vp]
         L.b200_tp_unique_id.argtypes = [vp]
         L.b200_tp_init.argtypes = [ctypes.POINTER(vp), vp, i32, i32, ctypes.c_uint32]
         L.b200_tp_init_from_nccl.argtypes = [ctypes.POINTER(vp), vp, ctypes.c_uint32]
@@ -468,6 +471,24 @@ def reduce_gather(slots, n_src: int, slot_rows: int, rows: int, cols: int, ld: i
     _check(lib().b200_reduce_gather_bf16(_dptr(slots), n_src, slot_rows, rows, cols, ld, arr,
                                          len(dst_ptrs), dst_row0, dst_ld, _stream(stream)),
            "b200_reduce_gather_bf16")
+
+
+def reduce_residual_adaln_gather(slots, n_src: int, slot_rows: int, rows: int, cols: int,
+                                 ld: int, x, gate, scale, dst_ptrs, dst_row0: int, dst_ld: int,
+                                 rows_per_mod: int = None, mod_stride: int = 0,
+                                 eps: float = 1e-6, stream=None):
+    """b200_reduce_residual_adaln_gather: sum the first `rows` rows of n_src bf16 slots,
+    x[:rows] += tanh(gate) * sum (f32 x, this owner's rows of the residual stream), then
+    bf16(LN(x) * (1 + scale)) broadcast to dst_ptrs at row dst_row0.  gate / scale: f32
+    [n_mod, cols] rows mod_stride apart (one row for every token when rows_per_mod is
+    None)."""
+    arr = _ptr_array(dst_ptrs)
+    if rows_per_mod is None:
+        rows_per_mod = 1 << 62
+    _check(lib().b200_reduce_residual_adaln_gather(
+        _dptr(slots), n_src, slot_rows, rows, cols, ld, _dptr(x), x.stride(0), _dptr(gate),
+        _dptr(scale), rows_per_mod, mod_stride, float(eps), arr, len(dst_ptrs), dst_row0,
+        dst_ld, _stream(stream)), "b200_reduce_residual_adaln_gather")
 
 
 def qkv_norm_rope_gemm(x, w_qkv, batch: int, tokens: int, heads: int, norm_q_w, norm_k_w, pe,

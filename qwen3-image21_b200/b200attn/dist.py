@@ -153,7 +153,18 @@ class ScatterOutProj:
                                   out_ptrs=[int(p) for p in h_out.buffer_ptrs]))
         self.calls = 0
 
-    def __call__(self, attn_local, w_out, h0: int, h1: int, head_dim: int = 128, status=None):
+    def own_rows(self, t: int):
+        """(first row, row count) of the output block this rank owns for t rows."""
+        r0 = self.rank * self.rows_per
+        return r0, max(0, min(self.rows_per, t - r0))
+
+    def __call__(self, attn_local, w_out, h0: int, h1: int, head_dim: int = 128, status=None,
+                 residual=None, eps: float = 1e-6):
+        """attn_local [t, (h1-h0)*head_dim] bf16 -> the full to_out product [t, hidden] bf16
+        on every rank.  With residual=(x_own, gate, scale) — x_own f32 [own rows, hidden],
+        this rank's rows of the residual stream (own_rows), gate / scale f32 [hidden] —
+        the owners apply x_own += tanh(gate) * sum and return LN(x) * (1 + scale) instead,
+        all-gathered (src/transformer.rs:411-418: the attention residual and norm2)."""
         import b200attn
         t = attn_local.shape[0]
         if t > self.rows or w_out.shape[0] != self.hidden:
@@ -164,9 +175,16 @@ class ScatterOutProj:
         b200attn.gemm_scatter(attn_local, w_cols, st["slot_ptrs"], self.rank, self.rows_per,
                               self.hidden, status=status)
         st["h"].barrier(channel=0, timeout_ms=self.timeout_ms)
-        r0 = self.rank * self.rows_per
-        mine = max(0, min(self.rows_per, t - r0))
-        b200attn.reduce_gather(st["slots"], self.world, self.rows_per, mine, self.hidden,
-                               self.hidden, st["out_ptrs"], r0, self.hidden)
+        r0, mine = self.own_rows(t)
+        if residual is None:
+            b200attn.reduce_gather(st["slots"], self.world, self.rows_per, mine, self.hidden,
+                                   self.hidden, st["out_ptrs"], r0, self.hidden)
+        else:
+            x_own, gate, scale = residual
+            if x_own.shape[0] < mine or x_own.shape[1] != self.hidden:
+                raise ValueError("x_own must hold this rank's rows of the residual stream")
+            b200attn.reduce_residual_adaln_gather(
+                st["slots"], self.world, self.rows_per, mine, self.hidden, self.hidden, x_own,
+                gate, scale, st["out_ptrs"], r0, self.hidden, eps=eps)
         st["h"].barrier(channel=0, timeout_ms=self.timeout_ms)
         return st["out"][:t]

@@ -897,8 +897,149 @@ __global__ void __launch_bounds__(256) reduce_gather_kernel(const uint4* slots, 
   __threadfence_system();
 }
 
+// The owner's step of the head-sharded block with the gated residual and the next
+// LayerNorm fused in (one CTA per row, 256 threads, columns in 8-element groups):
+//   sum   = sum over s of slots[s][r, :]              (bf16 partials, f32, fixed order)
+//   x[r]  = x[r] + tanh(gate[m]) * sum                (f32, in place: the owner's rows)
+//   y     = LN(x[r]) * (1 + scale[m])                 (bf16, written to every dst buffer)
+// with m = (row0 + r) / rows_per_mod the row's modulation row.  kNG = groups per thread.
+constexpr int kRrThreads = 256;
+
+__device__ __forceinline__ float rr_block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // red[] is reused by consecutive reductions
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kRrThreads / 32; ++w) t += red[w];
+  return t;
+}
+
+template <int kNG>
+__global__ void __launch_bounds__(kRrThreads) reduce_residual_adaln_gather_kernel(
+    const uint4* slots, int32_t n_src, int32_t rows, int32_t c8, int64_t ld8,
+    int64_t slot_stride8, float* x, int64_t ldx, const float* gate, const float* scale,
+    int64_t rows_per_mod, int64_t mod_stride, float eps, ReduceGatherDst dst) {
+  __shared__ float red[kRrThreads / 32];
+  const float inv_n = 1.f / static_cast<float>(c8 * 8);
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int64_t m = (dst.row0 + r) / rows_per_mod;
+    float xv[kNG][8];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNG; ++i) {
+      const int c = threadIdx.x + i * kRrThreads;
+      if (c < c8) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int k = 0; k < n_src; ++k) {  // fixed order: the sum does not depend on timing
+          const uint4 u = slots[k * slot_stride8 + r * ld8 + c];
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            acc[2 * e] += __uint_as_float(w[e] << 16);
+            acc[2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+          }
+        }
+        float4* xr = reinterpret_cast<float4*>(x + r * ldx + c * 8);
+        const float4* gr = reinterpret_cast<const float4*>(gate + m * mod_stride + c * 8);
+        const float4 x0 = xr[0], x1 = xr[1], g0 = gr[0], g1 = gr[1];
+        const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        const float gs[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          xv[i][e] = fmaf(tanhf(gs[e]), acc[e], xs[e]);
+          s += xv[i][e];
+        }
+        xr[0] = make_float4(xv[i][0], xv[i][1], xv[i][2], xv[i][3]);
+        xr[1] = make_float4(xv[i][4], xv[i][5], xv[i][6], xv[i][7]);
+      }
+    }
+    const float mean = rr_block_sum(s, red) * inv_n;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNG; ++i) {
+      const int c = threadIdx.x + i * kRrThreads;
+      if (c < c8) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = xv[i][e] - mean;
+          q += d * d;
+        }
+      }
+    }
+    const float rstd = rsqrtf(rr_block_sum(q, red) * inv_n + eps);
+#pragma unroll
+    for (int i = 0; i < kNG; ++i) {
+      const int c = threadIdx.x + i * kRrThreads;
+      if (c < c8) {
+        const float4* sr = reinterpret_cast<const float4*>(scale + m * mod_stride + c * 8);
+        const float4 s0 = sr[0], s1 = sr[1];
+        const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        uint32_t ow[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a = (xv[i][2 * e] - mean) * rstd * (1.f + ss[2 * e]);
+          const float b = (xv[i][2 * e + 1] - mean) * rstd * (1.f + ss[2 * e + 1]);
+          __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+          ow[e] = *reinterpret_cast<uint32_t*>(&v);
+        }
+        const uint4 o = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        const int64_t drow = dst.row0 + r;
+        for (int d = 0; d < dst.n; ++d) static_cast<uint4*>(dst.ptr[d])[drow * dst.ld8 + c] = o;
+      }
+    }
+  }
+  __threadfence_system();
+}
+
 }  // namespace
 }  // namespace b200
+
+extern "C" int b200_reduce_residual_adaln_gather(
+    const void* slots, int32_t n_src, int32_t slot_rows, int32_t rows, int32_t cols, int64_t ld,
+    float* x, int64_t ldx, const float* gate, const float* scale, int64_t rows_per_mod,
+    int64_t mod_stride, float eps, void* const* dst_bufs, int32_t n_dst, int64_t dst_row0,
+    int64_t dst_ld, b200_stream_t stream) {
+  if (!slots || n_src < 1 || rows < 0 || slot_rows < rows || cols <= 0 || cols % 8 != 0 ||
+      cols > 8192 || ld < cols || ld % 8 != 0)
+    return B200_ERR_INVALID;
+  if (!x || !gate || !scale || ldx < cols || ldx % 4 != 0 || rows_per_mod < 1 ||
+      mod_stride < 0 || mod_stride % 4 != 0 || !(eps >= 0.f))
+    return B200_ERR_INVALID;
+  if (!dst_bufs || n_dst < 1 || n_dst > kMaxOwners || dst_row0 < 0 || dst_ld < cols || dst_ld % 8 != 0)
+    return B200_ERR_INVALID;
+  const void* ptrs[] = {slots, x, gate, scale};
+  for (const void* q : ptrs)
+    if (reinterpret_cast<uintptr_t>(q) & 15u) return B200_ERR_INVALID;
+  ReduceGatherDst dst{};
+  for (int i = 0; i < n_dst; ++i) {
+    if (!dst_bufs[i] || (reinterpret_cast<uintptr_t>(dst_bufs[i]) & 15u)) return B200_ERR_INVALID;
+    dst.ptr[i] = dst_bufs[i];
+  }
+  dst.n = n_dst;
+  dst.row0 = dst_row0;
+  dst.ld8 = dst_ld / 8;
+  if (rows == 0) return B200_OK;
+  const int64_t cap = static_cast<int64_t>(gemm_sms()) * 8;
+  const unsigned grid = static_cast<unsigned>(rows < cap ? rows : cap);
+  const int c8 = cols / 8;
+  const int64_t sstride = static_cast<int64_t>(slot_rows) * (ld / 8);
+  auto* sl = static_cast<const uint4*>(slots);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (c8 <= kRrThreads)
+    reduce_residual_adaln_gather_kernel<1><<<grid, kRrThreads, 0, st>>>(
+        sl, n_src, rows, c8, ld / 8, sstride, x, ldx, gate, scale, rows_per_mod, mod_stride, eps, dst);
+  else if (c8 <= 2 * kRrThreads)
+    reduce_residual_adaln_gather_kernel<2><<<grid, kRrThreads, 0, st>>>(
+        sl, n_src, rows, c8, ld / 8, sstride, x, ldx, gate, scale, rows_per_mod, mod_stride, eps, dst);
+  else
+    reduce_residual_adaln_gather_kernel<4><<<grid, kRrThreads, 0, st>>>(
+        sl, n_src, rows, c8, ld / 8, sstride, x, ldx, gate, scale, rows_per_mod, mod_stride, eps, dst);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
 
 extern "C" int b200_reduce_gather_bf16(const void* slots, int32_t n_src, int32_t slot_rows,
                                        int32_t rows, int32_t cols, int64_t ld,

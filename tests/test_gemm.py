@@ -91,6 +91,49 @@ def test_scatter_gather_emulated_ranks(cuda, world, T):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("world,T,hidden,per_mod", [(2, 1000, 512, None), (4, 640, 3072, 160),
+                                                    (3, 257, 2048, 100)])
+def test_scatter_residual_adaln_emulated_ranks(cuda, world, T, hidden, per_mod):
+    """The head-sharded to_out with the gated residual and the next modulated LayerNorm
+    fused into the owners' step (src/transformer.rs:411-418), `world` ranks emulated on one
+    GPU: each owner's rows of x become x + tanh(gate) * attn_out in place, and every rank
+    receives LN(x) * (1 + scale) for all rows.  per_mod = rows sharing one modulation row
+    (one per batch item); None = one row for all tokens."""
+    g = torch.Generator(device=cuda).manual_seed(world * 7 + T)
+    H = 2 * world
+    attn = torch.randn(T, H * 128, generator=g, device=cuda).bfloat16()
+    w_out = (0.02 * torch.randn(hidden, H * 128, generator=g, device=cuda)).bfloat16()
+    x = torch.randn(T, hidden, generator=g, device=cuda)
+    n_mod = 1 if per_mod is None else -(-T // per_mod)
+    gate = torch.randn(n_mod, hidden, generator=g, device=cuda)
+    scale = 0.5 * torch.randn(n_mod, hidden, generator=g, device=cuda)
+    rows_per = -(-T // world)
+    slots = [torch.zeros(world * rows_per, hidden, dtype=torch.bfloat16, device=cuda) for _ in range(world)]
+    outs = [torch.zeros(world * rows_per, hidden, dtype=torch.bfloat16, device=cuda) for _ in range(world)]
+    x_own = [x[q * rows_per:(q + 1) * rows_per].clone() for q in range(world)]
+    hs = H // world
+    for r in range(world):
+        b200attn.gemm_scatter(attn[:, r * hs * 128:(r + 1) * hs * 128].contiguous(),
+                              w_out[:, r * hs * 128:(r + 1) * hs * 128],
+                              [t.data_ptr() for t in slots], r, rows_per, hidden)
+    for q in range(world):
+        mine = max(0, min(rows_per, T - q * rows_per))
+        b200attn.reduce_residual_adaln_gather(
+            slots[q], world, rows_per, mine, hidden, hidden, x_own[q], gate, scale,
+            [t.data_ptr() for t in outs], q * rows_per, hidden, rows_per_mod=per_mod,
+            mod_stride=hidden if per_mod else 0)
+    torch.cuda.synchronize()
+    m = torch.zeros(T, dtype=torch.long, device=cuda) if per_mod is None else \
+        torch.arange(T, device=cuda) // per_mod
+    x_want = x + torch.tanh(gate[m]) * (attn.float() @ w_out.float().t())
+    y_want = torch.nn.functional.layer_norm(x_want, (hidden,), eps=1e-6) * (1 + scale[m])
+    assert _rel(torch.cat(x_own)[:T], x_want) < 2e-3   # bf16 partials summed in f32
+    for q in range(world):
+        assert _rel(outs[q][:T].float(), y_want) < 6e-3
+        assert torch.equal(outs[q], outs[0])
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("B,T,H,C", [(1, 256, 2, 256), (3, 200, 4, 512), (2, 4096, 32, 4096)])
 def test_qkv_norm_rope_gemm_matches_unfused(cuda, B, T, H, C):
     """The fused Q/K/V projection (RMSNorm + RoPE in the epilogue) against the float32

@@ -109,6 +109,62 @@ def _rank_fused(rank, world, port, result_path):
         dist.destroy_process_group()
 
 
+def _rank_fused_residual(rank, world, port, result_path):
+    import torch
+    import torch.distributed as dist
+
+    from b200attn import dist as bdist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, device_id=dev)
+    try:
+        T, H, hidden = 1000, 8, 1024
+        g = torch.Generator().manual_seed(23)
+        attn = torch.randn(T, H * 128, generator=g).bfloat16().to(dev)
+        w_out = (0.02 * torch.randn(hidden, H * 128, generator=g)).bfloat16().to(dev)
+        x = torch.randn(T, hidden, generator=g).to(dev)
+        gate = torch.randn(1, hidden, generator=g).to(dev)
+        scale = (0.5 * torch.randn(1, hidden, generator=g)).to(dev)
+        h0, h1 = bdist.head_shard(H, world, rank)
+        fused = bdist.ScatterOutProj(T, hidden, dev)
+        r0, mine = fused.own_rows(T)
+        x_own = x[r0:r0 + mine].clone()
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+        out = fused(attn[:, h0 * 128:h1 * 128].contiguous(), w_out, h0, h1, status=st,
+                    residual=(x_own, gate, scale))
+        torch.cuda.synchronize()
+        x_want = x + torch.tanh(gate) * (attn.float() @ w_out.float().t())
+        y_want = torch.nn.functional.layer_norm(x_want, (hidden,), eps=1e-6) * (1 + scale)
+        rel_y = float((out.float() - y_want).norm() / y_want.norm())
+        xw = x_want[r0:r0 + mine]
+        rel_x = float((x_own - xw).norm() / xw.norm())
+        worst = bdist.max_over_ranks(max(rel_y, rel_x), device=dev)
+        bad = bdist.max_over_ranks(float(st.item()), device=dev)
+        if rank == 0:
+            with open(result_path, "w") as f:
+                f.write(f"{worst} {bad}")
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_scatter_out_proj_with_residual_and_norm_matches_single_gpu(tmp_path):
+    """The fused to_out with the attention residual and norm2 in the owners' step: each
+    rank's rows of the f32 residual stream are updated in place and every rank receives
+    the modulated LayerNorm of all rows (src/transformer.rs:411-418)."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    result = tmp_path / "fused_res.txt"
+    mp.spawn(_rank_fused_residual, args=(2, _free_port(), str(result)), nprocs=2, join=True)
+    worst, bad = map(float, result.read_text().split())
+    assert bad == 0
+    assert worst < 6e-3, worst
+
+
 def test_scatter_fused_out_proj_matches_single_gpu(tmp_path):
     """The to_out GEMM whose epilogue reduce-scatters over NVLink, then the owners' sum and
     broadcast: every rank ends with the full projection of all heads."""
