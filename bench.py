@@ -854,6 +854,23 @@ def run_head_sharded(args, cfg, rank, world, dev):
                     fused_then_residual_adaln=step_res_after(
                         lambda a: fused(a, w_out, h0, h1, status=status)),
                     nccl_then_residual_adaln=step_res_after(step_nccl_tail))
+        if T % world == 0:
+            # The same split with library collectives: reduce-scatter the partials, the
+            # residual and norm2 on this rank's rows, all-gather the normalised rows.
+            rows_n = T // world
+            x_n = x_full[rank * rows_n:(rank + 1) * rows_n].clone()
+            rs = torch.empty(rows_n, hidden, dtype=torch.bfloat16, device=dev)
+            y_n = torch.empty(rows_n, hidden, dtype=torch.bfloat16, device=dev)
+
+            def step_res_nccl_owner(mark=None):
+                part = bdist.out_proj_partial(attention(), w_out, h0, h1, HEAD_DIM)
+                dist.reduce_scatter_tensor(rs, part)
+                b200attn.residual_adaln(x_n, rs, gate, scale, y_n, rows_per_mod=T,
+                                        stream=stream)
+                dist.all_gather_into_tensor(y_full, y_n)
+                return y_full
+
+            legs["nccl_reduce_scatter_owner_all_gather"] = step_res_nccl_owner
         for fn in legs.values():
             for _ in range(2):
                 fn()
@@ -951,8 +968,10 @@ def run_head_sharded(args, cfg, rank, world, dev):
             "fused_path": {"ms_per_step": ms_fused, "how": fused_note},
             "with_residual_norm2": None if res_ms is None else dict(
                 res_ms, how=("step + x += tanh(gate1) * to_out + norm2 * (1 + scale2): in the "
-                             "owners' reduce step (owner_step) vs a residual_adaln kernel over "
-                             "all rows after the sum (ms per step, max over ranks)")),
+                             "owners' reduce step (owner_step); vs a residual_adaln kernel over "
+                             "all rows after the sum; vs NCCL reduce-scatter, residual_adaln on "
+                             "this rank's rows and NCCL all-gather (ms per step, max over "
+                             "ranks)")),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak,
                          # captured with all 32 heads on one GPU; a rank's launch moves its
