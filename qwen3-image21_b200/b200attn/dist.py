@@ -102,14 +102,20 @@ def head_sharded_attention_layer(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w
     return partial.reshape(b, t, -1)
 
 
-def prefer_fused_out_proj(world: int) -> bool:
-    """Whether ScatterOutProj beats a cuBLAS GEMM + NCCL all-reduce at this rank count.
+def prefer_fused_out_proj(world: int, residual: bool = False) -> bool:
+    """Whether ScatterOutProj beats a cuBLAS GEMM + NCCL collectives at this rank count.
 
-    Measured on 8x B200 (config 4, one block: attention + to_out + reduction, NCCL free to
-    use NVLS): 2 ranks 2.22 vs 2.32 ms, 4 ranks 1.46 vs 1.47 ms, 8 ranks 1.19 vs 1.00 ms.
-    At 8 ranks the to_out GEMM is small (K = 512) and NCCL's in-switch reduction moves the
-    partials faster than peer stores plus a gather."""
-    return 1 < world <= 4
+    Measured on B200 boxes (config 4, one block: attention + to_out + reduction, NCCL free
+    to use NVLS), fused vs NCCL all-reduce: 2 ranks 2.22 vs 2.32 ms and 2.28 vs 2.27 ms,
+    4 ranks 1.46 vs 1.47 ms, 8 ranks 1.19 vs 1.00 ms and 0.986 vs 0.993 ms (two builds of
+    the attention kernel): level within run-to-run noise at 8 ranks, so NCCL is kept
+    there.  With the block's residual and norm2 folded into the owners' step
+    (residual=True) the fused path wins at every rank count measured: 2 ranks 2.25 vs
+    2.68 ms, 8 ranks 0.985 ms vs 1.064 ms for NCCL reduce-scatter + residual on the
+    rank's rows + all-gather (src/transformer.rs:411-421)."""
+    if world <= 1:
+        return False
+    return True if residual else world <= 4
 
 
 class ScatterOutProj:

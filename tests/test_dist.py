@@ -28,6 +28,14 @@ def test_head_shard_partitions_heads(heads, world):
     assert max(sizes) - min(sizes) <= 1
 
 
+def test_prefer_fused_out_proj_follows_the_measured_crossover():
+    assert not bdist.prefer_fused_out_proj(1)
+    assert [bdist.prefer_fused_out_proj(n) for n in (2, 4, 8)] == [True, True, False]
+    # with the residual and norm2 in the owners' step the fused path won at every N
+    assert all(bdist.prefer_fused_out_proj(n, residual=True) for n in (2, 4, 8))
+    assert not bdist.prefer_fused_out_proj(1, residual=True)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
