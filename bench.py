@@ -772,7 +772,21 @@ def run_head_sharded(args, cfg, rank, world, dev):
                           "owner sum / broadcast kernel")
         except RuntimeError as e:
             fused_note = f"no symmetric memory ({e}); fused path = NCCL path"
-    use_fused = world == 1 or (fused is not None and bdist.prefer_fused_out_proj(world))
+    nvls = None
+    nvls_note = "one GPU"
+    if world > 1:
+        try:
+            nvls = bdist.NvlsOutProj(T, hidden, dev)
+            nvls_note = ("tcgen05 GEMM into this rank's buffer + owners' sum in the NVSwitch "
+                         "(multimem.ld_reduce) and broadcast (multimem.st)")
+        except RuntimeError as e:
+            nvls_note = f"unavailable: {e}"
+    path = bdist.out_proj_path(world)
+    if path == "nvls" and nvls is None:
+        path = "scatter"
+    if path == "scatter" and fused is None:
+        path = "nccl"
+    use_fused = world == 1 or path in ("scatter", "nvls")
     out_bf16 = torch.empty(T, hidden, dtype=torch.bfloat16, device=dev)
 
     def attention(mark=None):
@@ -801,6 +815,9 @@ def run_head_sharded(args, cfg, rank, world, dev):
     def step_nccl(mark=None):
         return step_nccl_tail(attention(mark))
 
+    def step_nvls(mark=None):
+        return nvls(attention(mark), w_out, h0, h1, status=status)
+
     def barrier():
         if world > 1:
             dist.barrier()
@@ -819,6 +836,8 @@ def run_head_sharded(args, cfg, rank, world, dev):
     for _ in range(args.warmup):
         step_fused()
         step_nccl()
+        if nvls is not None:
+            step_nvls()
     barrier()
     marks = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
@@ -826,6 +845,7 @@ def run_head_sharded(args, cfg, rank, world, dev):
         ms_fused = timed(step_fused, args.steps, marks)
     attn_ms = sum(m[0].elapsed_time(m[1]) for m in marks) / args.steps
     ms_nccl = timed(step_nccl, args.steps)
+    ms_nvls = timed(step_nvls, args.steps) if nvls is not None else None
     # ---- the block's next steps fused into the owners' step: x += tanh(gate1) * to_out and
     # norm2(x) * (1 + scale2) (src/transformer.rs:411-421).  Timed against the same work
     # done after the gather / all-reduce by the residual_adaln kernel over all T rows.
@@ -850,7 +870,12 @@ def run_head_sharded(args, cfg, rank, world, dev):
                 return y_full
             return run
 
-        legs = dict(owner_step=step_res_owner,
+        legs = {}
+        if nvls is not None:
+            x_nv = x_full[r0:r0 + mine].clone()
+            legs["nvls_owner_step"] = lambda mark=None: nvls(
+                attention(), w_out, h0, h1, status=status, residual=(x_nv, gate, scale))
+        legs.update(owner_step=step_res_owner,
                     fused_then_residual_adaln=step_res_after(
                         lambda a: fused(a, w_out, h0, h1, status=status)),
                     nccl_then_residual_adaln=step_res_after(step_nccl_tail))
@@ -906,7 +931,9 @@ def run_head_sharded(args, cfg, rank, world, dev):
             a = b200attn.attention_forward(di["q"], di["k"], di["v"], pk, pv, ones, ones, pe,
                                            out=attn, workspace=fwd_ws, status=status,
                                            stream=stream).view(T, hl * HEAD_DIM)
-            if fused is not None and use_fused:
+            if path == "nvls":
+                res = nvls(a, w_out, h0, h1, status=status)
+            elif fused is not None and use_fused:
                 res = fused(a, w_out, h0, h1, status=status)
             elif world == 1:
                 res = b200attn.gemm(a, w_cols, out=gemm_out[sl], status=status)
@@ -935,8 +962,10 @@ def run_head_sharded(args, cfg, rank, world, dev):
                    d2h=T * hidden * 2)
     ms_fused = bdist.max_over_ranks(ms_fused, device=dev)
     ms_nccl = bdist.max_over_ranks(ms_nccl, device=dev)
+    if ms_nvls is not None:
+        ms_nvls = bdist.max_over_ranks(ms_nvls, device=dev)
     e2e_ms = bdist.max_over_ranks(e2e["ms"], device=dev) if e2e else None
-    ms_step = ms_fused if use_fused else ms_nccl
+    ms_step = ms_nvls if path == "nvls" else ms_fused if use_fused else ms_nccl
     attn_ms = bdist.max_over_ranks(attn_ms, device=dev)
     if res_ms is not None:
         res_ms = {k: bdist.max_over_ranks(v, device=dev) for k, v in res_ms.items()}
@@ -959,13 +988,14 @@ def run_head_sharded(args, cfg, rank, world, dev):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) q/k/v and prefix cache, N(0,0.02) to_out)",
             "config": c4_config(cfg, world),
-            "sum_of_partials": (fused_note if use_fused else
-                                "cuBLAS + NCCL all-reduce (faster than the fused path at this "
-                                "rank count)"),
+            "sum_of_partials": (nvls_note if path == "nvls" else fused_note if use_fused else
+                                "cuBLAS + NCCL all-reduce (faster than the fused paths at "
+                                "this rank count)"),
             "nccl_path": {"ms_per_step": ms_nccl,
                           "value": (attn_flops + proj_flops) / (ms_nccl / 1e3) / 1e12,
                           "how": "cuBLAS to_out partial + NCCL all-reduce (bf16)"},
             "fused_path": {"ms_per_step": ms_fused, "how": fused_note},
+            "nvls_path": {"ms_per_step": ms_nvls, "how": nvls_note},
             "with_residual_norm2": None if res_ms is None else dict(
                 res_ms, how=("step + x += tanh(gate1) * to_out + norm2 * (1 + scale2): in the "
                              "owners' reduce step (owner_step); vs a residual_adaln kernel over "
@@ -993,6 +1023,7 @@ def run_head_sharded(args, cfg, rank, world, dev):
         }
         print(json.dumps(line), flush=True)
     del fused
+    del nvls
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -80,6 +80,26 @@ int b200_reduce_gather_bf16(const void* slots, int32_t n_src, int32_t slot_rows,
  * block, the sum of the to_out partials followed by `x + tanh(gate1) * attn` and
  * `norm2(x) * (1 + scale2)` (src/transformer.rs:196, 411-418).  cols % 8 == 0, cols <= 8192.
  */
+/*
+ * The owner's step with the reduction done by the NVSwitch.  mc_part / mc_out are CUDA
+ * multicast addresses (cuMulticast objects, e.g. torch symmetric memory's multicast_ptr)
+ * bound to every rank's bf16 partial [*, part_ld] and output [*, out_ld] buffers.  For
+ * r < rows, row g = row0 + r:
+ *   sum    = multimem.ld_reduce add over the ranks of part[g, :]  (f32 accumulate, bf16)
+ *   x == NULL:  out[g, :] = sum                                    on every rank
+ *   else:       x[r, :] += tanh(gate[m, :]) * sum ;  out[g, :] = bf16(LN(x[r]) (1 + scale[m]))
+ * with m = g / rows_per_mod, as b200_reduce_residual_adaln_gather.  Every rank's partial
+ * must be complete (a barrier) before the call and every owner's call must finish (a
+ * barrier) before `out` is read.  Per GPU, NVLink carries (1 + 1/N) partials each way
+ * instead of the 2 (N-1)/N of the scatter / gather pair, so it pays from N = 4 up.
+ * The result is deterministic up to the switch's reduction order.  cols % 8 == 0,
+ * cols <= 8192; 16-byte aligned addresses.
+ */
+int b200_reduce_nvls(const void* mc_part, int64_t part_ld, void* mc_out, int64_t out_ld,
+                     int64_t row0, int32_t rows, int32_t cols, float* x, int64_t ldx,
+                     const float* gate, const float* scale, int64_t rows_per_mod,
+                     int64_t mod_stride, float eps, b200_stream_t stream);
+
 int b200_reduce_residual_adaln_gather(const void* slots, int32_t n_src, int32_t slot_rows,
                                       int32_t rows, int32_t cols, int64_t ld, float* x,
                                       int64_t ldx, const float* gate, const float* scale,

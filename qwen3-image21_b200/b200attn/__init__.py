@@ -38,6 +38,7 @@ EXPORTED = (
     "b200_residual_adaln", "b200_swiglu",
     "b200_dequant_q4_k", "b200_dequant_q6_k", "b200_wait_selftest", "b200_gemm",
     "b200_gemm_scatter", "b200_reduce_gather_bf16", "b200_reduce_residual_adaln_gather",
+    "b200_reduce_nvls",
     "b200_qkv_norm_rope_gemm",
     "b200_tp_unique_id", "b200_tp_init", "b200_tp_init_from_nccl", "b200_tp_rank", "b200_tp_size",
     "b200_tp_out_proj_allreduce", "b200_tp_wait", "b200_tp_destroy",
@@ -108,6 +109,8 @@ def lib() -> ctypes.CDLL:
         L.b200_reduce_gather_bf16.argtypes = [vp, i32, i32, i32, i32, i64, vp, i32, i64, i64, vp]
         L.b200_reduce_residual_adaln_gather.argtypes = [vp, i32, i32, i32, i32, i64, vp, i64, vp, vp,
                                                         i64, i64, f32, vp, i32, i64, i64, vp]
+        L.b200_reduce_nvls.argtypes = [vp, i64, vp, i64, i64, i32, i32, vp, i64, vp, vp, i64, i64,
+                                       f32, vp]
         L.b200_tp_unique_id.argtypes = [vp]
         L.b200_tp_init.argtypes = [ctypes.POINTER(vp), vp, i32, i32, ctypes.c_uint32]
         L.b200_tp_init_from_nccl.argtypes = [ctypes.POINTER(vp), vp, ctypes.c_uint32]
@@ -489,6 +492,20 @@ def reduce_residual_adaln_gather(slots, n_src: int, slot_rows: int, rows: int, c
         _dptr(slots), n_src, slot_rows, rows, cols, ld, _dptr(x), x.stride(0), _dptr(gate),
         _dptr(scale), rows_per_mod, mod_stride, float(eps), arr, len(dst_ptrs), dst_row0,
         dst_ld, _stream(stream)), "b200_reduce_residual_adaln_gather")
+
+
+def reduce_nvls(mc_part: int, part_ld: int, mc_out: int, out_ld: int, row0: int, rows: int,
+                cols: int, x=None, gate=None, scale=None, rows_per_mod: int = None,
+                mod_stride: int = 0, eps: float = 1e-6, stream=None):
+    """b200_reduce_nvls: rows [row0, row0 + rows) of every rank's partial summed by the
+    NVSwitch (multicast addresses mc_part / mc_out, ints), optionally x += tanh(gate) * sum
+    and LN(x) * (1 + scale) (x: this owner's f32 rows), written to every rank's output."""
+    if rows_per_mod is None:
+        rows_per_mod = 1 << 62
+    _check(lib().b200_reduce_nvls(
+        mc_part, part_ld, mc_out, out_ld, row0, rows, cols, _dptr(x),
+        0 if x is None else x.stride(0), _dptr(gate), _dptr(scale), rows_per_mod, mod_stride,
+        float(eps), _stream(stream)), "b200_reduce_nvls")
 
 
 def qkv_norm_rope_gemm(x, w_qkv, batch: int, tokens: int, heads: int, norm_q_w, norm_k_w, pe,

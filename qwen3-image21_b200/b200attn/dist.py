@@ -102,20 +102,32 @@ def head_sharded_attention_layer(q, k, v, prefix_k, prefix_v, norm_q_w, norm_k_w
     return partial.reshape(b, t, -1)
 
 
-def prefer_fused_out_proj(world: int, residual: bool = False) -> bool:
-    """Whether ScatterOutProj beats a cuBLAS GEMM + NCCL collectives at this rank count.
+def out_proj_path(world: int, residual: bool = False) -> str:
+    """How to sum the head-sharded to_out partials at this rank count: "scatter"
+    (ScatterOutProj: peer stores from the GEMM epilogue, owners' sum and broadcast),
+    "nvls" (NvlsOutProj: owners' sum in the NVSwitch) or "nccl" (cuBLAS + all-reduce).
 
-    Measured on B200 boxes (config 4, one block: attention + to_out + reduction, NCCL free
-    to use NVLS), fused vs NCCL all-reduce: 2 ranks 2.22 vs 2.32 ms and 2.28 vs 2.27 ms,
-    4 ranks 1.46 vs 1.47 ms, 8 ranks 1.19 vs 1.00 ms and 0.986 vs 0.993 ms (two builds of
-    the attention kernel): level within run-to-run noise at 8 ranks, so NCCL is kept
-    there.  With the block's residual and norm2 folded into the owners' step
-    (residual=True) the fused path wins at every rank count measured: 2 ranks 2.25 vs
-    2.68 ms, 8 ranks 0.985 ms vs 1.064 ms for NCCL reduce-scatter + residual on the
-    rank's rows + all-gather (src/transformer.rs:411-421)."""
+    Measured on B200 boxes, config 4 (one block: attention + to_out + the sum), ms:
+      2 ranks: scatter 2.18-2.28, NCCL 2.27-2.32, NVLS 2.58;
+               with residual + norm2: scatter 2.25-2.37, NVLS 2.59, NCCL RS/AG 2.67
+      4 ranks: scatter 1.46, NCCL 1.47 (NVLS not measured; by bytes moved it is between)
+      8 ranks: NVLS 0.975, scatter 0.986-0.987, NCCL 0.991-0.993;
+               with residual + norm2: NVLS 0.981, scatter 0.985-0.989, NCCL RS/AG 1.063
+    At 2 ranks NVLS moves more bytes than peer stores ((1 + 1/N) against 2 (N-1)/N
+    partials each way); at 8 fewer."""
     if world <= 1:
-        return False
-    return True if residual else world <= 4
+        return "local"
+    if world >= 8:
+        return "nvls"
+    if residual:
+        return "scatter"
+    return "scatter" if world <= 4 else "nccl"
+
+
+def prefer_fused_out_proj(world: int, residual: bool = False) -> bool:
+    """Whether one of this library's fused paths (scatter or NVLS) beats cuBLAS + NCCL at
+    this rank count (out_proj_path)."""
+    return out_proj_path(world, residual) in ("scatter", "nvls")
 
 
 class ScatterOutProj:
@@ -192,5 +204,78 @@ class ScatterOutProj:
             b200attn.reduce_residual_adaln_gather(
                 st["slots"], self.world, self.rows_per, mine, self.hidden, self.hidden, x_own,
                 gate, scale, st["out_ptrs"], r0, self.hidden, eps=eps)
+        st["h"].barrier(channel=0, timeout_ms=self.timeout_ms)
+        return st["out"][:t]
+
+
+class NvlsOutProj:
+    """Head-sharded to_out with the sum of the partials done by the NVSwitch (NVLS).
+
+    Each rank's GEMM writes its full partial [T, hidden] into its own symmetric buffer
+    (local stores only); after a barrier, owner q reads rows [q*rows_per, ...) of all
+    ranks' partials summed in the switch (b200_reduce_nvls: multimem.ld_reduce through the
+    partial buffers' multicast address), optionally applies the block's residual and
+    norm2, and writes each row once to the output buffers' multicast address, which puts
+    it in every rank's output; a second barrier ends the call.  Per GPU the links carry
+    (1 + 1/N) partials each way, against 2 (N-1)/N for ScatterOutProj's peer stores, so
+    this path is for N >= 4.  Same call contract, buffer alternation and returned view as
+    ScatterOutProj.  Raises RuntimeError when the buffers have no multicast address (no
+    NVSwitch multicast on this system)."""
+
+    def __init__(self, rows: int, hidden: int, device, group=None, timeout_ms: int = 10000):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rows_per = -(-rows // self.world)
+        self.rows, self.hidden, self.timeout_ms = rows, hidden, timeout_ms
+        self.sets = []
+        for _ in range(2):
+            part = symm_mem.empty(self.world * self.rows_per, hidden, dtype=torch.bfloat16,
+                                  device=device)
+            out = symm_mem.empty(self.world * self.rows_per, hidden, dtype=torch.bfloat16,
+                                 device=device)
+            h_part = symm_mem.rendezvous(part, group)
+            h_out = symm_mem.rendezvous(out, group)
+            mc_part, mc_out = int(h_part.multicast_ptr), int(h_out.multicast_ptr)
+            if not mc_part or not mc_out:
+                raise RuntimeError("symmetric memory has no multicast address on this system")
+            for h, t in ((h_part, part), (h_out, out)):
+                # the multicast address must map the tensor from its first element
+                if int(h.buffer_ptrs[self.rank]) != t.data_ptr() or int(getattr(h, "offset", 0)):
+                    raise RuntimeError("symmetric tensor does not start its buffer")
+            self.sets.append(dict(part=part, out=out, h=h_out, mc_part=mc_part, mc_out=mc_out))
+        self.calls = 0
+
+    def own_rows(self, t: int):
+        """(first row, row count) of the output block this rank owns for t rows."""
+        r0 = self.rank * self.rows_per
+        return r0, max(0, min(self.rows_per, t - r0))
+
+    def __call__(self, attn_local, w_out, h0: int, h1: int, head_dim: int = 128, status=None,
+                 residual=None, eps: float = 1e-6):
+        """As ScatterOutProj.__call__ (residual=(x_own, gate, scale) folds in the block's
+        attention residual and norm2, src/transformer.rs:411-421)."""
+        import b200attn
+        t = attn_local.shape[0]
+        if t > self.rows or w_out.shape[0] != self.hidden:
+            raise ValueError("shape does not fit the buffers")
+        st = self.sets[self.calls % 2]
+        self.calls += 1
+        w_cols = w_out[:, h0 * head_dim:h1 * head_dim]
+        b200attn.gemm(attn_local, w_cols, out=st["part"][:t], status=status)
+        st["h"].barrier(channel=0, timeout_ms=self.timeout_ms)
+        r0, mine = self.own_rows(t)
+        if residual is None:
+            b200attn.reduce_nvls(st["mc_part"], self.hidden, st["mc_out"], self.hidden, r0, mine,
+                                 self.hidden)
+        else:
+            x_own, gate, scale = residual
+            if x_own.shape[0] < mine or x_own.shape[1] != self.hidden:
+                raise ValueError("x_own must hold this rank's rows of the residual stream")
+            b200attn.reduce_nvls(st["mc_part"], self.hidden, st["mc_out"], self.hidden, r0, mine,
+                                 self.hidden, x=x_own, gate=gate, scale=scale, eps=eps)
         st["h"].barrier(channel=0, timeout_ms=self.timeout_ms)
         return st["out"][:t]

@@ -995,8 +995,171 @@ __global__ void __launch_bounds__(kRrThreads) reduce_residual_adaln_gather_kerne
   __threadfence_system();
 }
 
+// The owner's step with the reduction in the NVSwitch (NVLS): every rank's full partial
+// sits in its own buffer, bound with the others to one CUDA multicast object; the owner
+// reads its rows through the multicast address with multimem.ld_reduce (the switch adds
+// the N ranks' bf16 values, accumulating in f32, and returns the sum rounded to bf16
+// once), applies the optional residual and norm2 exactly as
+// reduce_residual_adaln_gather_kernel does, and writes each result row once with
+// multimem.st to the output's multicast address, which lands it in every rank's buffer.
+// Per GPU the links carry its partial out once and the other owners' rows in once,
+// (1 + 1/N) x the partial each way, against 2 (N-1)/N x for peer stores.
+__device__ __forceinline__ uint4 mc_ld_reduce_bf16x8(const void* addr) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void mc_st_16b(void* addr, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr),
+               "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+               "f"(__uint_as_float(v.w))
+               : "memory");
+}
+
+struct NvlsArgs {
+  const uint4* mc_part;  // multicast address of the partial buffers, 8 bf16 per uint4
+  uint4* mc_out;         // multicast address of the output buffers
+  int64_t row0, part_ld8, out_ld8;
+  int32_t rows, c8;
+  float* x;              // this owner's f32 rows, or null: no residual / norm
+  int64_t ldx;
+  const float* gate;
+  const float* scale;
+  int64_t rows_per_mod, mod_stride;
+  float eps;
+};
+
+template <int kNG>
+__global__ void __launch_bounds__(kRrThreads) reduce_nvls_kernel(const NvlsArgs a) {
+  __shared__ float red[kRrThreads / 32];
+  const float inv_n = 1.f / static_cast<float>(a.c8 * 8);
+  for (int64_t r = blockIdx.x; r < a.rows; r += gridDim.x) {
+    const int64_t grow = a.row0 + r;
+    uint4 sum[kNG];
+#pragma unroll
+    for (int i = 0; i < kNG; ++i) {
+      const int c = threadIdx.x + i * kRrThreads;
+      if (c < a.c8) sum[i] = mc_ld_reduce_bf16x8(a.mc_part + grow * a.part_ld8 + c);
+    }
+    if (!a.x) {  // the sum alone, broadcast
+#pragma unroll
+      for (int i = 0; i < kNG; ++i) {
+        const int c = threadIdx.x + i * kRrThreads;
+        if (c < a.c8) mc_st_16b(a.mc_out + grow * a.out_ld8 + c, sum[i]);
+      }
+      continue;  // uniform over the CTA
+    }
+    const int64_t m = grow / a.rows_per_mod;
+    float xv[kNG][8];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNG; ++i) {
+      const int c = threadIdx.x + i * kRrThreads;
+      if (c < a.c8) {
+        const uint32_t w[4] = {sum[i].x, sum[i].y, sum[i].z, sum[i].w};
+        float4* xr = reinterpret_cast<float4*>(a.x + r * a.ldx + c * 8);
+        const float4* gr = reinterpret_cast<const float4*>(a.gate + m * a.mod_stride + c * 8);
+        const float4 x0 = xr[0], x1 = xr[1], g0 = gr[0], g1 = gr[1];
+        const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        const float gs[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float y = __uint_as_float((e & 1) ? (w[e >> 1] & 0xffff0000u) : (w[e >> 1] << 16));
+          xv[i][e] = fmaf(tanhf(gs[e]), y, xs[e]);
+          s += xv[i][e];
+        }
+        xr[0] = make_float4(xv[i][0], xv[i][1], xv[i][2], xv[i][3]);
+        xr[1] = make_float4(xv[i][4], xv[i][5], xv[i][6], xv[i][7]);
+      }
+    }
+    const float mean = rr_block_sum(s, red) * inv_n;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNG; ++i) {
+      const int c = threadIdx.x + i * kRrThreads;
+      if (c < a.c8) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = xv[i][e] - mean;
+          q += d * d;
+        }
+      }
+    }
+    const float rstd = rsqrtf(rr_block_sum(q, red) * inv_n + a.eps);
+#pragma unroll
+    for (int i = 0; i < kNG; ++i) {
+      const int c = threadIdx.x + i * kRrThreads;
+      if (c < a.c8) {
+        const float4* sr = reinterpret_cast<const float4*>(a.scale + m * a.mod_stride + c * 8);
+        const float4 s0 = sr[0], s1 = sr[1];
+        const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        uint32_t ow[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          __nv_bfloat162 v = __floats2bfloat162_rn((xv[i][2 * e] - mean) * rstd * (1.f + ss[2 * e]),
+                                                   (xv[i][2 * e + 1] - mean) * rstd * (1.f + ss[2 * e + 1]));
+          ow[e] = *reinterpret_cast<uint32_t*>(&v);
+        }
+        mc_st_16b(a.mc_out + grow * a.out_ld8 + c, make_uint4(ow[0], ow[1], ow[2], ow[3]));
+      }
+    }
+  }
+  asm volatile("fence.proxy.alias;" ::: "memory");
+  __threadfence_system();
+}
+
 }  // namespace
 }  // namespace b200
+
+extern "C" int b200_reduce_nvls(const void* mc_part, int64_t part_ld, void* mc_out,
+                                int64_t out_ld, int64_t row0, int32_t rows, int32_t cols,
+                                float* x, int64_t ldx, const float* gate, const float* scale,
+                                int64_t rows_per_mod, int64_t mod_stride, float eps,
+                                b200_stream_t stream) {
+  if (!mc_part || !mc_out || row0 < 0 || rows < 0 || cols <= 0 || cols % 8 != 0 ||
+      cols > 8192 || part_ld < cols || part_ld % 8 != 0 || out_ld < cols || out_ld % 8 != 0)
+    return B200_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(mc_part) & 15u) || (reinterpret_cast<uintptr_t>(mc_out) & 15u))
+    return B200_ERR_INVALID;
+  if (x) {
+    if (!gate || !scale || ldx < cols || ldx % 4 != 0 || rows_per_mod < 1 || mod_stride < 0 ||
+        mod_stride % 4 != 0 || !(eps >= 0.f))
+      return B200_ERR_INVALID;
+    const void* ptrs[] = {x, gate, scale};
+    for (const void* q : ptrs)
+      if (reinterpret_cast<uintptr_t>(q) & 15u) return B200_ERR_INVALID;
+  }
+  if (rows == 0) return B200_OK;
+  NvlsArgs a{};
+  a.mc_part = static_cast<const uint4*>(mc_part);
+  a.mc_out = static_cast<uint4*>(mc_out);
+  a.row0 = row0;
+  a.part_ld8 = part_ld / 8;
+  a.out_ld8 = out_ld / 8;
+  a.rows = rows;
+  a.c8 = cols / 8;
+  a.x = x;
+  a.ldx = ldx;
+  a.gate = gate;
+  a.scale = scale;
+  a.rows_per_mod = rows_per_mod < 1 ? 1 : rows_per_mod;
+  a.mod_stride = mod_stride;
+  a.eps = eps;
+  const int64_t cap = static_cast<int64_t>(gemm_sms()) * 8;
+  const unsigned grid = static_cast<unsigned>(rows < cap ? rows : cap);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (a.c8 <= kRrThreads)
+    reduce_nvls_kernel<1><<<grid, kRrThreads, 0, st>>>(a);
+  else if (a.c8 <= 2 * kRrThreads)
+    reduce_nvls_kernel<2><<<grid, kRrThreads, 0, st>>>(a);
+  else
+    reduce_nvls_kernel<4><<<grid, kRrThreads, 0, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+}
 
 extern "C" int b200_reduce_residual_adaln_gather(
     const void* slots, int32_t n_src, int32_t slot_rows, int32_t rows, int32_t cols, int64_t ld,

@@ -28,12 +28,14 @@ def test_head_shard_partitions_heads(heads, world):
     assert max(sizes) - min(sizes) <= 1
 
 
-def test_prefer_fused_out_proj_follows_the_measured_crossover():
+def test_out_proj_path_follows_the_measured_crossover():
+    assert bdist.out_proj_path(1) == "local"
+    assert [bdist.out_proj_path(n) for n in (2, 4, 8)] == ["scatter", "scatter", "nvls"]
+    assert [bdist.out_proj_path(n, residual=True) for n in (2, 4, 8)] == \
+        ["scatter", "scatter", "nvls"]
+    # a fused path won at every rank count measured
+    assert all(bdist.prefer_fused_out_proj(n, residual=r) for n in (2, 4, 8) for r in (0, 1))
     assert not bdist.prefer_fused_out_proj(1)
-    assert [bdist.prefer_fused_out_proj(n) for n in (2, 4, 8)] == [True, True, False]
-    # with the residual and norm2 in the owners' step the fused path won at every N
-    assert all(bdist.prefer_fused_out_proj(n, residual=True) for n in (2, 4, 8))
-    assert not bdist.prefer_fused_out_proj(1, residual=True)
 
 
 def _free_port():

@@ -165,6 +165,80 @@ def test_scatter_out_proj_with_residual_and_norm_matches_single_gpu(tmp_path):
     assert worst < 6e-3, worst
 
 
+def _rank_nvls(rank, world, port, result_path):
+    import torch
+    import torch.distributed as dist
+
+    from b200attn import dist as bdist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, device_id=dev)
+    try:
+        T, H, hidden = 1000, 8, 1024
+        g = torch.Generator().manual_seed(29)
+        attn = torch.randn(T, H * 128, generator=g).bfloat16().to(dev)
+        w_out = (0.02 * torch.randn(hidden, H * 128, generator=g)).bfloat16().to(dev)
+        x = torch.randn(T, hidden, generator=g).to(dev)
+        gate = torch.randn(1, hidden, generator=g).to(dev)
+        scale = (0.5 * torch.randn(1, hidden, generator=g)).to(dev)
+        h0, h1 = bdist.head_shard(H, world, rank)
+        try:
+            proj = bdist.NvlsOutProj(T, hidden, dev)
+        except RuntimeError as e:   # no multicast on this system: every rank says so
+            if rank == 0:
+                with open(result_path, "w") as f:
+                    f.write("skip " + str(e).replace(" ", "_"))
+            dist.barrier()
+            return
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+        a_loc = attn[:, h0 * 128:h1 * 128].contiguous()
+        want = attn.float() @ w_out.float().t()
+        rels = []
+        for _ in range(2):   # the plain sum, twice (both buffer sets)
+            out = proj(a_loc, w_out, h0, h1, status=st)
+            torch.cuda.synchronize()
+            rels.append(float((out.float() - want).norm() / want.norm()))
+        r0, mine = proj.own_rows(T)
+        x_own = x[r0:r0 + mine].clone()
+        out = proj(a_loc, w_out, h0, h1, status=st, residual=(x_own, gate, scale))
+        torch.cuda.synchronize()
+        # the switch returns the sum rounded to bf16 once; the reference adds that to x
+        s_bf16 = want.bfloat16().float()
+        x_want = x + torch.tanh(gate) * s_bf16
+        y_want = torch.nn.functional.layer_norm(x_want, (hidden,), eps=1e-6) * (1 + scale)
+        rels.append(float((out.float() - y_want).norm() / y_want.norm()))
+        xw = x_want[r0:r0 + mine]
+        rels.append(float((x_own - xw).norm() / xw.norm()))
+        worst = bdist.max_over_ranks(max(rels), device=dev)
+        bad = bdist.max_over_ranks(float(st.item()), device=dev)
+        if rank == 0:
+            with open(result_path, "w") as f:
+                f.write(f"{worst} {bad}")
+        del proj
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nvls_out_proj_matches_single_gpu(tmp_path):
+    """to_out with the partials summed in the NVSwitch (multimem.ld_reduce) and the rows
+    broadcast by multimem.st, with and without the residual / norm2 step."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    result = tmp_path / "nvls.txt"
+    mp.spawn(_rank_nvls, args=(2, _free_port(), str(result)), nprocs=2, join=True)
+    text = result.read_text()
+    if text.startswith("skip"):
+        pytest.skip(text)
+    worst, bad = map(float, text.split())
+    assert bad == 0
+    assert worst < 6e-3, worst
+
+
 def test_scatter_fused_out_proj_matches_single_gpu(tmp_path):
     """The to_out GEMM whose epilogue reduce-scatters over NVLink, then the owners' sum and
     broadcast: every rank ends with the full projection of all heads."""
