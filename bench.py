@@ -113,6 +113,9 @@ def parse_args():
                     help="config 5: prompts in the batch (default 8; fewer only for profiling)")
     ap.add_argument("--gemm", choices=["cublas", "b200"], default="cublas",
                     help="config 5: the block linears' GEMM (cuBLAS or the tcgen05 kernel)")
+    ap.add_argument("--dequant-sweep", action="store_true",
+                    help="config 5: time Q4_K dequantisation + GEMM against the bf16 GEMM "
+                         "for one block's gate_up linear over M = 16 ... 65536 rows, then exit")
     ap.add_argument("--fused-qkv", action="store_true",
                     help="config 5: Q/K/V projections with norm + RoPE in the GEMM epilogue")
     ap.add_argument("--no-weight-prefetch", action="store_true",
@@ -427,6 +430,9 @@ def main():
     cfg = CONFIGS[args.config]
     if args.config == "c4":
         run_head_sharded(args, cfg, rank, world, dev)
+        return
+    if args.config == "c5" and args.dequant_sweep:
+        dequant_sweep(dev)
         return
     if args.config == "c5":
         run_denoise(args, cfg, rank, world, dev)
@@ -1068,6 +1074,79 @@ def c5_flops(model_cfg, lengths, T):
     lin += 2.0 * T * len(lengths) * model_cfg.hidden * model_cfg.in_channels * 2  # img_in, proj_out
     attn = sum(4.0 * model_cfg.heads * T * (n + T) * HEAD_DIM for n in lengths) * model_cfg.layers
     return lin, attn
+
+
+def dequant_sweep(dev, ms=(1, 2, 16, 64, 256, 1024, 4096, 16384, 65536), reps=20):
+    """Config 5's largest linear (gate_up: [2 x 12288, 4096], Q4_K) at M token rows: the
+    large-M path (dequantise into a bf16 scratch, then cuBLAS) against cuBLAS on a resident
+    bf16 weight, the fused few-row product (b200_kquant_gemv, M <= 2: the path of the
+    timestep and modulation linears), and the floor of a fused dequantising GEMM (its Q4_K
+    bytes at the measured copy bandwidth, or its FLOPs at the burst bf16 peak, whichever is
+    larger).  The Q4_K bytes (57 MB) fit in L2 across repetitions.  One JSON line."""
+    import torch
+    import b200attn
+    from b200attn import gguf
+    from b200attn.mmdit import MMDiTConfig
+    mc = MMDiTConfig()
+    n, k = 2 * mc.ffn, mc.hidden
+    g = torch.Generator(device=dev).manual_seed(11)
+    w = (0.02 * torch.randn(n, k, generator=g, device=dev)).to(torch.bfloat16)
+    blocks = gguf.quantize(w, "q4_k")
+    ql = gguf.QuantLinear(blocks, "q4_k", (n, k))
+    scratch = torch.empty(n, k, dtype=torch.bfloat16, device=dev)
+    w_dq = ql.dequant_into(scratch).clone()
+    pk_d, _src = peaks()
+    hbm = float(pk_d.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    peak = float(pk_d.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        """Device time per call: `reps` calls captured in one CUDA graph and replayed (the
+        Python launch cost of a call exceeds these kernels' run time)."""
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        stream.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        del graph
+        return e0.elapsed_time(e1) / reps
+
+    rows = []
+    for m in ms:
+        x = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        t_dq_gemm = timed(lambda: torch.matmul(x, ql.dequant_into(scratch).t(), out=y))
+        t_gemm = timed(lambda: torch.matmul(x, w_dq.t(), out=y))
+        t_dq = timed(lambda: ql.dequant_into(scratch))
+        floor_ms = max(blocks.numel() / (hbm * 1e9), 2.0 * m * n * k / (peak * 1e12)) * 1e3
+        t_gemv = None
+        if m <= b200attn.KQUANT_GEMV_MAX_ROWS:
+            xf = x.float()
+            yf = torch.empty(m, n, dtype=torch.float32, device=dev)
+            t_gemv = round(timed(lambda: ql.matvec(xf, out=yf)), 4)
+        rows.append({"m": m, "fused_gemv_ms": t_gemv, "dequant_then_gemm_ms": round(t_dq_gemm, 4),
+                     "bf16_gemm_ms": round(t_gemm, 4), "dequant_ms": round(t_dq, 4),
+                     "fused_floor_ms": round(floor_ms, 4),
+                     "overhead_vs_bf16": round(t_dq_gemm / t_gemm - 1.0, 3),
+                     "over_fused_floor": round(t_dq_gemm / floor_ms, 2)})
+    print(json.dumps({"dequant_sweep": {
+        "linear": f"gate_up [{n}, {k}] Q4_K ({blocks.numel()} bytes)", "rows": rows,
+        "how": "CUDA events around a CUDA graph of 20 calls (after 3 warm-up calls); GEMM = "
+               "cuBLAS (torch.matmul) bf16"}}),
+        flush=True)
 
 
 def run_denoise(args, cfg, rank, world, dev, leg=False):

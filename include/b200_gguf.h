@@ -45,6 +45,24 @@ int b200_dequant_q4_k(const void* blocks, void* out, int64_t n_blocks, b200_stre
 /* n_blocks consecutive Q6_K super-blocks -> out[n_blocks * 256] bf16. */
 int b200_dequant_q6_k(const void* blocks, void* out, int64_t n_blocks, b200_stream_t stream);
 
+#define B200_KQUANT_Q4_K 0
+#define B200_KQUANT_Q6_K 1
+#define B200_KQUANT_GEMV_MAX_ROWS 2
+
+/*
+ * y[i, j] = sum_k x[i, k] * W[j, k] for i < m <= 2, j < n: the weight W [n, k] is n rows
+ * of k / 256 consecutive super-blocks of `qtype` (Q4_K or Q6_K, the GGUF tensor's bytes),
+ * expanded in registers to exactly the bf16 values the dequantisation above writes, and
+ * never written out; products and sums in f32.  x: f32 rows ldx apart; y: f32 rows ldy apart.  The weight is read once,
+ * so at a few rows the product costs about its quantised bytes at HBM speed.  Replaces
+ * candle's QMatMul::forward on a batch of a few rows (src/quantized_transformer.rs:20-33:
+ * the timestep embedder and the modulation linear run at one row per sequence).
+ * k % 256 == 0.  B200_ERR_INVALID for m > 2: from a few rows on, the expansion work
+ * repeated per row makes the dequantisation above plus a tensor-core GEMM faster.
+ */
+int b200_kquant_gemv(const float* x, int64_t ldx, const void* blocks, int32_t qtype, float* y,
+                     int64_t ldy, int32_t m, int32_t n, int32_t k, b200_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,7 +38,7 @@ EXPORTED = (
     "b200_residual_adaln", "b200_swiglu",
     "b200_dequant_q4_k", "b200_dequant_q6_k", "b200_wait_selftest", "b200_gemm",
     "b200_gemm_scatter", "b200_reduce_gather_bf16", "b200_reduce_residual_adaln_gather",
-    "b200_reduce_nvls",
+    "b200_reduce_nvls", "b200_kquant_gemv",
     "b200_qkv_norm_rope_gemm",
     "b200_tp_unique_id", "b200_tp_init", "b200_tp_init_from_nccl", "b200_tp_rank", "b200_tp_size",
     "b200_tp_out_proj_allreduce", "b200_tp_wait", "b200_tp_destroy",
@@ -111,6 +111,7 @@ def lib() -> ctypes.CDLL:
                                                         i64, i64, f32, vp, i32, i64, i64, vp]
         L.b200_reduce_nvls.argtypes = [vp, i64, vp, i64, i64, i32, i32, vp, i64, vp, vp, i64, i64,
                                        f32, vp]
+        L.b200_kquant_gemv.argtypes = [vp, i64, vp, i32, vp, i64, i32, i32, i32, vp]
         L.b200_tp_unique_id.argtypes = [vp]
         L.b200_tp_init.argtypes = [ctypes.POINTER(vp), vp, i32, i32, ctypes.c_uint32]
         L.b200_tp_init_from_nccl.argtypes = [ctypes.POINTER(vp), vp, ctypes.c_uint32]
@@ -492,6 +493,23 @@ def reduce_residual_adaln_gather(slots, n_src: int, slot_rows: int, rows: int, c
         _dptr(slots), n_src, slot_rows, rows, cols, ld, _dptr(x), x.stride(0), _dptr(gate),
         _dptr(scale), rows_per_mod, mod_stride, float(eps), arr, len(dst_ptrs), dst_row0,
         dst_ld, _stream(stream)), "b200_reduce_residual_adaln_gather")
+
+
+KQUANT_TYPES = {"q4_k": 0, "q6_k": 1}
+KQUANT_GEMV_MAX_ROWS = 2
+
+
+def kquant_gemv(x, blocks, qtype: str, n: int, out=None, stream=None):
+    """b200_kquant_gemv: x f32 [m, k] (m <= 2) times the k-quant weight [n, k] (GGUF
+    super-blocks, uint8 [n, k / 256 * block bytes]) transposed -> f32 [m, n]."""
+    import torch
+    m, k = x.shape
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    _check(lib().b200_kquant_gemv(_dptr(x), x.stride(0), _dptr(blocks), KQUANT_TYPES[qtype],
+                                  _dptr(out), out.stride(0), m, n, k, _stream(stream)),
+           "b200_kquant_gemv")
+    return out
 
 
 def reduce_nvls(mc_part: int, part_ld: int, mc_out: int, out_ld: int, row0: int, rows: int,

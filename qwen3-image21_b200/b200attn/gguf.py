@@ -119,3 +119,10 @@ class QuantLinear:
 
     def nbytes(self) -> int:
         return self.blocks.numel()
+
+    def matvec(self, x, out=None, stream=None):
+        """x f32 [m, in_features] (m <= 2) -> f32 [m, out_features] = x W^T, the weight
+        expanded in registers (b200_kquant_gemv), never written out."""
+        import b200attn
+        return b200attn.kquant_gemv(x, self.blocks, self.qtype, self.shape[0], out=out,
+                                    stream=stream)

@@ -190,9 +190,12 @@ class MMDiT:
                  prefetch_weights: bool = True):
         """weight_format "bf16" keeps the block linears in bf16; "q4_k_m" stores them as GGUF
         Q4_K / Q6_K super-blocks (llama.cpp's Q4_K_M rule) and dequantises each block's six
-        matrices to a bf16 scratch right before its GEMMs.  The other weights (img_in,
-        txt_in, timestep, modulation, norm_out, proj_out: 1 % of the parameters) stay
-        bf16 / f32 either way.  fused_qkv: a cached step runs the Q/K/V projections with the
+        matrices to a bf16 scratch right before its GEMMs; the timestep embedder's two
+        linears and the modulation linear become Q4_K too and run as one-row products
+        straight from the super-blocks (b200_kquant_gemv), as the reference's GGUF model
+        runs them through QMatMul (src/quantized_transformer.rs:37-53, 216-228).  The
+        other weights (img_in, txt_in, norm_out, proj_out) stay bf16 / f32 either way, as
+        the GGUF files the reference reads store them unquantised.  fused_qkv: a cached step runs the Q/K/V projections with the
         Q/K RMSNorm + RoPE in the GEMM epilogue (b200_qkv_norm_rope_gemm) and then the
         attention kernel alone; otherwise (the default, 1.3 % faster at config 5 while the
         tcgen05 GEMM runs the 12288-wide projection at ~90 % of cuBLAS) three cuBLAS GEMMs
@@ -238,8 +241,12 @@ class MMDiT:
         for blk in self.blocks:  # [to_q ; to_k ; to_v] stacked: one GEMM for the fused path
             blk["wqkv"] = torch.cat([blk.pop("wq"), blk.pop("wk"), blk.pop("wv")], 0).contiguous()
             blk["wq"], blk["wk"], blk["wv"] = (blk["wqkv"][j * h:(j + 1) * h] for j in range(3))
+        self.q_time = None
         if weight_format == "q4_k_m":
             from b200attn import gguf as bq
+            self.q_time = {k: bq.QuantLinear(bq.quantize(w, "q4_k"), "q4_k", tuple(w.shape))
+                           for k, w in (("t1", self.t1), ("t2", self.t2), ("mod", self.mod_w))}
+            del self.t1, self.t2, self.mod_w
             # reference names of the block linears (the fused gate_up is one GGUF tensor in
             # ComfyUI-style files, src/quantized_transformer.rs:160-166, output [gate; up])
             names = dict(wq="to_q", wk="to_k", wv="to_v", wo="to_out", wgp="gate_up", wmo="out")
@@ -279,25 +286,33 @@ class MMDiT:
         return [(self._buf(f"stage_{tag}_k{j}", tuple(shape), torch.bfloat16),
                  self._buf(f"stage_{tag}_v{j}", tuple(shape), torch.bfloat16)) for j in range(2)]
 
+    def _linear_f32(self, x, name):
+        """x f32 [k] @ W^T for the timestep / modulation linears: f32 weights, or (q4_k_m)
+        the Q4_K super-blocks through b200_kquant_gemv."""
+        if self.q_time is not None:
+            return self.q_time[name].matvec(x.reshape(1, -1).contiguous())[0]
+        return x @ {"t1": self.t1, "t2": self.t2, "mod": self.mod_w}[name].t()
+
+    def _time_proj(self, e):
+        import torch.nn.functional as F
+        return self._linear_f32(F.silu(self._linear_f32(e, "t1")), "t2")
+
     def time_embed(self, t: float):
         """QwenTimestepProj (src/transformer.rs:112-114) of timestep_embedding(t) -> f32 [hidden]."""
         import torch
-        import torch.nn.functional as F
-        e = torch.from_numpy(timestep_embedding(t)).to(self.device)
-        return F.silu(e @ self.t1.t()) @ self.t2.t()
+        return self._time_proj(torch.from_numpy(timestep_embedding(t)).to(self.device))
 
     def zero_time_embed(self):
         """t_emb of the t = 0 sinusoid [1]*128 + [0]*128 (src/transformer.rs:715-727)."""
         import torch
-        import torch.nn.functional as F
         e = torch.cat([torch.ones(T_DIM // 2), torch.zeros(T_DIM // 2)]).to(self.device)
-        return F.silu(e @ self.t1.t()) @ self.t2.t()
+        return self._time_proj(e)
 
     def modulation(self, t_emb):
         """Modulation::forward (src/transformer.rs:357-359): [4 * hidden] f32, chunks
         (scale1, gate1, scale2, gate2)."""
         import torch.nn.functional as F
-        return F.silu(t_emb) @ self.mod_w.t()
+        return self._linear_f32(F.silu(t_emb), "mod")
 
     def final_scale(self, t_emb):
         """FinalLayer's scale (src/transformer.rs:450): linear(silu(t_emb))."""
@@ -349,6 +364,12 @@ class MMDiT:
         out = {k: v.detach().float().cpu() for k, v in weights.items()}
         if self.weight_format == "bf16":
             return out
+        for key, name in (("t1", "time_text_embed.timestep_embedder.linear_1.weight"),
+                          ("t2", "time_text_embed.timestep_embedder.linear_2.weight"),
+                          ("mod", "modulation.1.weight")):
+            ql = self.q_time[key]
+            out[name] = ql.dequant_into(torch.empty(ql.shape, dtype=torch.bfloat16,
+                                                    device=self.device)).float().cpu()
         names = dict(wq="attn.to_q", wk="attn.to_k", wv="attn.to_v", wo="attn.to_out.0",
                      wmo="img_mlp.out")
         f = self.cfg.ffn

@@ -18,6 +18,10 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 FIX = np.load(os.path.join(ROOT, "tests", "golden", "gguf_kquants.npz"))
 
 
+def _rel(a, b):
+    return float((a.double() - b.double()).norm() / b.double().norm())
+
+
 def bf16_bits(x: np.ndarray) -> np.ndarray:
     """float32 -> bf16 bit patterns, round to nearest even (finite inputs)."""
     u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
@@ -69,7 +73,43 @@ def test_dequant_rejects_bad_arguments():
     assert L.b200_dequant_q6_k(16, 16, 0, None) == b200attn.OK
 
 
+def test_kquant_gemv_rejects_bad_arguments():
+    L = b200attn.lib()
+    Q4 = b200attn.KQUANT_TYPES["q4_k"]
+    assert L.b200_kquant_gemv(16, 256, 16, Q4, 16, 64, 0, 64, 256, None) == b200attn.OK  # m = 0
+    assert L.b200_kquant_gemv(16, 256, 16, Q4, 16, 64, 3, 64, 256, None) == b200attn.ERR_INVALID
+    assert L.b200_kquant_gemv(16, 300, 16, Q4, 16, 64, 2, 64, 300, None) == b200attn.ERR_INVALID
+    assert L.b200_kquant_gemv(16, 256, 16, 7, 16, 64, 2, 64, 256, None) == b200attn.ERR_INVALID
+    assert L.b200_kquant_gemv(16, 128, 16, Q4, 16, 64, 2, 64, 256, None) == b200attn.ERR_INVALID
+    assert L.b200_kquant_gemv(16, 256, 8, Q4, 16, 64, 2, 64, 256, None) == b200attn.ERR_INVALID
+    assert L.b200_kquant_gemv(None, 256, 16, Q4, 16, 64, 2, 64, 256, None) == b200attn.ERR_INVALID
+
+
 # ----------------------------------------------------------------------------- GPU
+@pytest.mark.gpu
+@pytest.mark.parametrize("qtype", ["q4_k", "q6_k"])
+@pytest.mark.parametrize("m,n,k,pad", [(1, 4096, 4096, 0), (2, 33, 256, 0), (1, 96, 8192, 64),
+                                       (2, 1000, 2048, 0), (2, 64, 12288, 256), (1, 40, 768, 0)])
+def test_kquant_gemv_matches_dequantized_matmul(cuda, qtype, m, n, k, pad):
+    """The fused few-row product straight from the super-blocks equals x times the
+    dequantised bf16 weight (the oracle's f32 dequantisation rounded to bf16), summed in
+    float64, to f32 accumulation accuracy: ragged row counts, x rows wider than k (pad),
+    k split into several shared-memory chunks of 8 super-blocks (k = 8192, 12288) or ending
+    in a partial one (k = 768: 3 blocks, whose Q6_K rows are only 2-byte aligned)."""
+    g = torch.Generator(device=cuda).manual_seed(m * 1000 + n)
+    w = torch.randn(n, k, generator=g, device=cuda) * 0.02
+    blocks = bq.quantize(w, qtype)
+    x_full = torch.randn(m, k + pad, generator=g, device=cuda)
+    x = x_full[:, :k]
+    got = bq.QuantLinear(blocks, qtype, (n, k)).matvec(x)
+    torch.cuda.synchronize()
+    deq = G.dequantize_q4_k if qtype == "q4_k" else G.dequantize_q6_k
+    w_bf16 = torch.from_numpy(deq(blocks.cpu().numpy()).reshape(n, k)).bfloat16().double()
+    want = x.cpu().double() @ w_bf16.t()
+    assert got.shape == (m, n)
+    assert _rel(got.cpu(), want) <= 1e-5
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("qtype", ["q4_k", "q6_k"])
 def test_cuda_dequant_bit_exact_on_fixture(cuda, qtype):
@@ -99,10 +139,6 @@ def test_cuda_dequant_bit_exact_at_size(cuda, qtype):
 
 TINY = mmdit.MMDiTConfig(layers=2, heads=2, text_dim=256)
 GRID = (16, 16)
-
-
-def _rel(a, b):
-    return float((a.double() - b.double()).norm() / b.double().norm())
 
 
 @pytest.mark.gpu
