@@ -25,6 +25,46 @@ def test_gemm_rejects_bad_arguments():
     assert L.b200_gemm(*args(m=0)) == b200attn.OK
 
 
+def test_owner_steps_reject_bad_arguments():
+    """The owners' reduce steps validate every argument before touching memory (the
+    addresses below are never dereferenced); rows = 0 with valid arguments is a no-op."""
+    import ctypes
+    L = b200attn.lib()
+    INV, OK = b200attn.ERR_INVALID, b200attn.OK
+    dst = (ctypes.c_void_p * 2)(4096, 8192)
+
+    def rr(slots=16, n_src=2, slot_rows=8, rows=0, cols=64, ld=64, x=16, ldx=64, gate=16,
+           scale=16, rpm=1 << 62, ms=0, eps=1e-6, n_dst=2, row0=0, dst_ld=64):
+        return L.b200_reduce_residual_adaln_gather(slots, n_src, slot_rows, rows, cols, ld, x,
+                                                   ldx, gate, scale, rpm, ms, eps, dst, n_dst,
+                                                   row0, dst_ld, None)
+    assert rr() == OK
+    assert rr(cols=60, ld=64, ldx=64, dst_ld=64) == INV       # cols % 8
+    assert rr(cols=8200, ld=8200, ldx=8200, dst_ld=8200) == INV  # > 8192 columns
+    assert rr(slot_rows=4, rows=8) == INV                     # rows beyond a slot
+    assert rr(ldx=62) == INV                                  # f32 rows not 16-byte vectors
+    assert rr(x=8) == INV                                     # misaligned residual rows
+    assert rr(gate=None) == INV
+    assert rr(ms=6) == INV                                    # modulation stride % 4
+    assert rr(eps=-1.0) == INV
+    assert rr(n_dst=9) == INV                                 # more owners than supported
+    assert rr(dst_ld=32) == INV                               # dst rows narrower than cols
+
+    def nv(mc_part=16, part_ld=64, mc_out=32, out_ld=64, row0=0, rows=0, cols=64, x=None,
+           ldx=0, gate=None, scale=None, rpm=1 << 62, ms=0, eps=1e-6):
+        return L.b200_reduce_nvls(mc_part, part_ld, mc_out, out_ld, row0, rows, cols, x, ldx,
+                                  gate, scale, rpm, ms, eps, None)
+    assert nv() == OK                                          # plain sum, no rows
+    assert nv(x=16, ldx=64, gate=16, scale=16) == OK          # with the residual step
+    assert nv(cols=60, part_ld=64, out_ld=64) == INV
+    assert nv(mc_part=8) == INV                                # misaligned multicast address
+    assert nv(part_ld=32) == INV
+    assert nv(row0=-1) == INV
+    assert nv(x=16, ldx=62, gate=16, scale=16) == INV
+    assert nv(x=16, ldx=64, gate=None, scale=16) == INV
+    assert nv(x=16, ldx=64, gate=16, scale=16, eps=-1.0) == INV
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (300, 512, 200), (1000, 96, 520),
                                    (4096, 4096, 4096), (16384, 4096, 512), (77, 12288, 4096)])
